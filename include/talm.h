@@ -1,0 +1,161 @@
+/*
+ * talm.h - C ABI of libtalm_b200.so, the sm_100a kernels behind the two hot paths of
+ * otarernazar-eng/Talm's QLoRA step:
+ *
+ *   (1) the vocabulary-sliced fused LM head + cross-entropy (reference: solution/fused_head.py)
+ *   (2) the grouped / per-projection NF4 dequantisation (reference: solution/qgroup.py,
+ *       solution/nf4_dequant.py)
+ *
+ * Conventions shared by every entry point:
+ *   - plain pointers to device memory and sizes; no framework types;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = the legacy default stream);
+ *   - every call is asynchronous on `stream`: it validates its arguments on the host,
+ *     enqueues its kernels and returns; it never synchronises, never allocates device memory
+ *     (the caller passes any workspace) and keeps no pointer after it returns;
+ *   - the return value is a TALM_* status; 0 means the work was enqueued. talm_last_error()
+ *     gives a one-line reason for the last non-zero status on the calling thread.
+ *   - fp16 tensors are passed as uint16_t* (IEEE binary16 bit patterns).
+ */
+#ifndef TALM_H_
+#define TALM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TALM_OK 0
+#define TALM_EINVAL 1   /* an argument violates a documented precondition */
+#define TALM_ECUDA 2    /* a CUDA runtime call or kernel launch failed */
+#define TALM_ERANGE 3   /* a size beyond what the kernels support */
+#define TALM_ENODEV 4   /* no sm_100 device is current */
+#define TALM_ETIMEOUT 5 /* a device-side wait gave up (read back by talm_device_status) */
+
+/* ABI version of this header (bumped on any signature change). */
+int talm_abi_version(void);
+
+/* One-line reason for the last non-zero status returned on this thread ("" if none). */
+const char* talm_last_error(void);
+
+/* Human-readable name of a status code. */
+const char* talm_status_string(int status);
+
+/* Reads and clears the device-side status word that kernels with bounded waits set when a
+ * wait gives up (TALM_OK when nothing was recorded). Synchronises the current device. No
+ * reference counterpart: the reference's Triton kernels have no device-side waits. */
+int talm_device_status(int* status_out);
+
+/* ------------------------------------------------------------------------------------------
+ * NF4 dequantisation
+ * ---------------------------------------------------------------------------------------- */
+
+/* Per-projection NF4 -> fp16 with an fp32 absmax per block.
+ * Replaces: solution/nf4_dequant.py:83-91 `nf4_dequantize(packed, absmax, blocksize, out)`
+ * (kernel `nf4_dequant_pairs_kernel`, nf4_dequant.py:38-80).
+ *   packed   : n_elems/2 bytes; byte i holds element 2i in its high nibble, 2i+1 in its low one
+ *   absmax   : ceil(n_elems / blocksize) fp32 scales
+ *   out      : n_elems fp16, out[e] = fp16(NF4[code(e)] * absmax[e / blocksize]) (fp32 product,
+ *              one round-to-nearest-even to fp16)
+ * Preconditions: n_elems even and >= 0, blocksize even and >= 2. Any alignment is accepted;
+ * the fast path needs packed 4-byte and out 16-byte aligned. */
+int talm_nf4_dequantize(const uint8_t* packed, const float* absmax, int64_t n_elems,
+                        int64_t blocksize, uint16_t* out, void* stream);
+
+/* Grouped NF4 -> fp16 over a layer's packed buffers with double-quantised absmax: one launch
+ * for the seven projections of a decoder layer.
+ * Replaces: solution/qgroup.py:94-99 `launch(packed, absmax8, code, absmax2, offset2, levels,
+ * out, n_rows, qblock, qblock2)` (kernel `nf4_group_dequant_kernel`, qgroup.py:72-91).
+ *   row r (one absmax block of qblock weights) has the scale
+ *     scale[r] = fp32(fp32(code[absmax8[r]] * absmax2[r / qblock2]) + offset2[r / qblock2])
+ *   (two separate roundings, no fused multiply-add), and
+ *     out[r*qblock + 2j]   = fp16(levels[packed[r*qblock/2 + j] >> 4] * scale[r])
+ *     out[r*qblock + 2j+1] = fp16(levels[packed[r*qblock/2 + j] & 15] * scale[r])
+ *   packed : n_rows*qblock/2 bytes     absmax8 : n_rows bytes        code : 256 fp32
+ *   absmax2, offset2 : ceil(n_rows / qblock2) fp32                  levels : 16 fp32
+ * Preconditions: qblock even, qblock/2 a power of two, n_rows*qblock/2 < 2^31, qblock2 >= 1. */
+int talm_nf4_group_dequant(const uint8_t* packed, const uint8_t* absmax8, const float* code,
+                           const float* absmax2, const float* offset2, const float* levels,
+                           uint16_t* out, int64_t n_rows, int64_t qblock, int64_t qblock2,
+                           void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Fused LM head + cross-entropy (vocabulary-sliced, no materialised logits)
+ * ---------------------------------------------------------------------------------------- */
+
+/* Per-row statistics, one float[TALM_HEAD_STATS] record per token row, relative to the part of
+ * the vocabulary a call covered (all of it on one GPU, the rank's shard under vocabulary
+ * parallelism). Argmax and the target logit are over fp16-rounded logits, as the reference's
+ * cuBLAS fp16 GEMM output (solution/fused_head.py:136-169). */
+#define TALM_HEAD_STATS 8
+#define TALM_STAT_M 0      /* running max of z                                      */
+#define TALM_STAT_S 1      /* sum exp(z - m)                                         */
+#define TALM_STAT_T 2      /* sum exp(z - m) * z                                     */
+#define TALM_STAT_ZT 3     /* z[target] if the target column is covered, else 0       */
+#define TALM_STAT_BEST 4   /* max z (same as m, kept for the argmax key)               */
+#define TALM_STAT_IDX 5    /* first global column attaining BEST, as int32 bits        */
+#define TALM_STAT_HIT 6    /* 1.0 if the target column is covered by the call, else 0  */
+#define TALM_STAT_PAD 7
+
+/* Device bytes of workspace talm_head_shard needs. */
+int talm_head_workspace_size(int64_t n_tokens, int64_t n_grad, int64_t hidden,
+                             int64_t vocab_cols, int64_t vocab_chunk, size_t* bytes);
+
+/* Logits GEMM + online log-sum-exp / entropy numerator / argmax / target logit over the
+ * vocabulary columns [vocab_col0, vocab_col0 + vocab_cols) of the weight, in slices of
+ * vocab_chunk columns, and (n_grad > 0) the accumulator acc[i] = sum_v exp(z_iv - m_i) W[v]
+ * of the first n_grad rows (the labelled rows, placed first by the caller).
+ * Replaces the slice loop of solution/fused_head.py:356-371 (`torch.mm` logits GEMM,
+ * `fused_head_vocab_kernel` stats mode :126-182, `torch.addmm` accumulator GEMM).
+ *   hidden  : fp16 [n_tokens, hidden], row stride ld_hidden elements
+ *   weight  : fp16 rows [vocab_cols, hidden] of this call's columns (pointer to row vocab_col0
+ *             is NOT implied: `weight` points at the first row of the covered range), row
+ *             stride ld_weight elements
+ *   targets : int64 [n_tokens] global column ids, negative = ignored row
+ *   stats   : float [n_tokens, TALM_HEAD_STATS] (written)
+ *   acc     : float [n_grad, hidden] (written when n_grad > 0)
+ * Preconditions: hidden % 8 == 0 and ld_* % 8 == 0 (16-byte rows for TMA), hidden/weight
+ * 16-byte aligned, 0 <= n_grad <= n_tokens, vocab_chunk >= 1, ws_bytes >=
+ * talm_head_workspace_size(...). */
+int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* weight,
+                    int64_t ld_weight, const int64_t* targets, int64_t n_tokens, int64_t n_grad,
+                    int64_t hidden_size, int64_t vocab_cols, int64_t vocab_col0,
+                    int64_t vocab_chunk, float* stats, float* acc, void* workspace,
+                    size_t ws_bytes, void* stream);
+
+/* Per-row outputs and the hidden gradient from complete statistics (one shard covering the
+ * whole vocabulary, or the combination of all shards).
+ * Replaces the last-slice branch of `fused_head_vocab_kernel` (fused_head.py:160-169) and its
+ * finalize mode (fused_head.py:111-125).
+ *   token_loss[i]    = labelled ? log(s) + m - zt : 0
+ *   token_entropy[i] = m + log(s) - t / s
+ *   correct[i]       = labelled && idx == target
+ *   grad ([n_tokens, hidden], fp16, or fp32 when grad_is_f32 != 0; skipped when NULL):
+ *     grad[i] = labelled && i < n_grad ? acc[i] * acc_scale[i] - fp16(W[target_i]) : 0
+ *     with acc_scale[i] = 1/s when acc_scale == NULL.
+ *   weight/ld_weight/vocab_col0: the rows of the vocabulary range the caller owns; the
+ *   subtraction of W[target] is done only for targets inside [vocab_col0, vocab_col0 +
+ *   vocab_cols) (the owning rank under vocabulary parallelism).
+ *   grad_rows (optional): output row of compacted row i (the inverse of the labelled-first
+ *   order); NULL = identity. */
+int talm_head_finalize(const float* stats, const int64_t* targets, int64_t n_tokens,
+                       int64_t n_grad, const float* acc, const float* acc_scale,
+                       const uint16_t* weight, int64_t ld_weight, int64_t vocab_col0,
+                       int64_t vocab_cols, int64_t hidden_size, const int64_t* grad_rows,
+                       float* token_loss, float* token_entropy, int32_t* correct,
+                       void* grad, int grad_is_f32, void* stream);
+
+/* Merges the statistics of n_shards vocabulary shards (gathered as [n_shards, n_tokens,
+ * TALM_HEAD_STATS], shard r covering the columns of rank r) into one record per row, and
+ * writes acc_scale[i] = exp(m_rank - M) / S for this rank's accumulator rows (n_grad rows).
+ * No reference counterpart: the reference is single-GPU; this is the exchange step of the
+ * vocabulary-parallel head (log-sum-exp merge of online-softmax partials). */
+int talm_head_combine(const float* gathered, int64_t n_shards, int64_t n_tokens, int64_t rank,
+                      int64_t n_grad, float* stats_out, float* acc_scale, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TALM_H_ */

@@ -1,0 +1,122 @@
+// C ABI plumbing shared by the kernels: status strings, the per-thread last error, the device
+// status word of bounded waits, device queries and the TMA descriptor encoder (driver entry
+// point fetched through the runtime, so the library loads on machines without a driver).
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "common.cuh"
+
+namespace talm {
+
+static thread_local char t_last_error[512] = "";
+
+int set_error(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int check_launch(const char* what) {
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) {
+    return set_error(TALM_ECUDA, "%s: %s", what, cudaGetErrorString(err));
+  }
+  return TALM_OK;
+}
+
+int current_sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  return n;
+}
+
+bool device_is_sm100() {
+  int dev = 0, major = 0, minor = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+    return false;
+  if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+    return false;
+  return major == 10 && minor == 0;
+}
+
+}  // namespace talm
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+  }
+  return fn;
+}
+
+int talm_make_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                          uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return talm::set_error(TALM_ENODEV, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    return talm::set_error(TALM_EINVAL, "TMA base address %p is not 16-byte aligned", base);
+  if ((row_stride_elems * 2) % 16 != 0)
+    return talm::set_error(TALM_EINVAL, "TMA row stride of %llu fp16 is not a multiple of 16 B",
+                           (unsigned long long)row_stride_elems);
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_elems * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return talm::set_error(TALM_EINVAL, "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu",
+                           (int)r, (unsigned long long)inner, (unsigned long long)outer);
+  return TALM_OK;
+}
+
+extern "C" {
+
+int talm_abi_version(void) { return 1; }
+
+const char* talm_last_error(void) { return talm::t_last_error; }
+
+const char* talm_status_string(int status) {
+  switch (status) {
+    case TALM_OK: return "ok";
+    case TALM_EINVAL: return "invalid argument";
+    case TALM_ECUDA: return "CUDA error";
+    case TALM_ERANGE: return "size out of range";
+    case TALM_ENODEV: return "no sm_100 device";
+    case TALM_ETIMEOUT: return "device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+int talm_device_status(int* status_out) {
+  if (status_out == nullptr) return talm::set_error(TALM_EINVAL, "status_out is NULL");
+  cudaError_t err = cudaDeviceSynchronize();
+  if (err != cudaSuccess)
+    return talm::set_error(TALM_ECUDA, "synchronize: %s", cudaGetErrorString(err));
+  int value = 0, zero = 0;
+  err = cudaMemcpyFromSymbol(&value, talm::g_device_status, sizeof(int));
+  if (err == cudaSuccess) err = cudaMemcpyToSymbol(talm::g_device_status, &zero, sizeof(int));
+  if (err != cudaSuccess)
+    return talm::set_error(TALM_ECUDA, "device status: %s", cudaGetErrorString(err));
+  *status_out = value;
+  return TALM_OK;
+}
+
+}  // extern "C"

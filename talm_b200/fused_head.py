@@ -1,0 +1,212 @@
+"""Fused output head + causal-LM loss on sm_100a, without a [N, V] logits tensor (drop-in for
+solution/fused_head.py).
+
+`fused_head_loss(hidden, weight, targets, num_items=None, vocab_chunk=None, *, token_chunk=None,
+n_labelled=None)` returns (loss, token_loss[N], token_entropy[N], correct[N]) with the
+reference's semantics (fused_head.py:53-58, :447-462):
+
+  loss      = sum over labelled t of (lse_t - z[t, y_t]) / num_items (or / #labelled)
+  entropy_t = lse_t - sum_v softmax(z_t)_v z_tv, for every row
+  correct_t = argmax_v z_tv == y_t (first column on ties), labelled rows only
+  z         = fp16(h16 . W16^T), the logits as the reference's fp16 cuBLAS GEMM rounds them
+
+and the hidden gradient computed in the same forward (dH = softmax(z) W16 - W16[y]), saved for a
+backward that only scales it (fused_head.py:280-287). The whole vocabulary walk runs in
+libtalm_b200 (csrc/head.cu): per slice a tcgen05 logits GEMM with the statistics fused into
+its epilogue, a per-row merge, and a tcgen05 accumulator GEMM over the labelled rows. The host
+code here keeps the reference's contract around it: the labelled-first row order
+(`labelled_first`), the denominator, the autograd Function and the module switches.
+"""
+
+import os
+
+import torch
+
+from . import _lib
+from .engaged import FELL_BACK, RAN
+
+BLOCK_V = 4096            # reference row-kernel block; kept for callers reading it
+NUM_WARPS = 8
+DEFAULT_CHUNK = 256
+VOCAB_CHUNK = int(os.environ.get("SOLUTION_HEAD_VCHUNK", "8192"))
+BLOCK_H = 512
+VOCAB_PATH = os.environ.get("SOLUTION_DISABLE_HEAD_VCHUNK") != "1"
+COMPACT = os.environ.get("SOLUTION_DISABLE_HEAD_COMPACT") != "1"
+ROW_UNIT = 1 if os.environ.get("SOLUTION_DISABLE_HEAD_ROWS") == "1" else 8
+
+
+def _denominator(num_items, labelled_count):
+    """solution/fused_head.py:272-277."""
+    if num_items is None:
+        return labelled_count.clamp(min=1).to(torch.float32)
+    if torch.is_tensor(num_items):
+        return num_items.to(device=labelled_count.device, dtype=torch.float32)
+    return torch.tensor(float(num_items), device=labelled_count.device)
+
+
+def _head_backward(ctx, grad_loss):
+    """dH * grad_loss / denom, 0 when denom == 0, in the hidden's dtype (fused_head.py:280-287)."""
+    (grad_hidden,) = ctx.saved_tensors
+    scale = grad_loss.to(torch.float32) / ctx.denom
+    scale = torch.where(ctx.denom != 0, scale, 0.0)
+    return (grad_hidden.to(torch.float32) * scale).to(ctx.out_dtype)
+
+
+def labelled_first(labelled, n_labelled):
+    """The order that puts the labelled rows first, each group in its original order, without a
+    host sync: (dest, src) with input row r at position dest[r] of the reordered rows and src the
+    inverse (fused_head.py:290-299)."""
+    n = labelled.shape[0]
+    pos = torch.arange(n, device=labelled.device)
+    seen = torch.cumsum(labelled, 0)
+    dest = torch.where(labelled, seen - 1, pos - seen + n_labelled)
+    src = torch.empty_like(dest).index_copy_(0, dest, pos)
+    return dest, src
+
+
+def _pad8(n):
+    return (n + 7) // 8 * 8
+
+
+def _operand(t, cols):
+    """fp16 rows usable by TMA: 16-byte aligned base, row stride a multiple of 8 elements,
+    `cols` (>= the tensor's width, a multiple of 8) addressable columns. Views when the tensor
+    already is one; a zero-padded fp16 copy otherwise (odd widths, fp32/bf16 storage, rows
+    that are not contiguous)."""
+    rows, width = t.shape
+    if (t.dtype == torch.float16 and t.stride(1) == 1 and width == cols
+            and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0):
+        return t, t.stride(0)
+    out = torch.zeros(rows, cols, dtype=torch.float16, device=t.device)
+    out[:, :width].copy_(t)
+    return out, cols
+
+
+def _check_cuda(*tensors):
+    for t in tensors:
+        if torch.is_tensor(t) and not t.is_cuda:
+            raise RuntimeError("fused_head_loss runs on CUDA tensors only (sm_100a kernels; "
+                               "there is no CPU path)")
+
+
+def head_forward(h16, w16, ld_w, targets, n_grad, hidden_cols, vocab_chunk, grad_rows=None,
+                 want_grad=True):
+    """The C-ABI call sequence of one single-GPU head: talm_head_shard over the whole vocabulary,
+    then talm_head_finalize. h16 [N, hidden_cols] fp16 TMA rows, w16 [V, >= hidden_cols] fp16
+    rows with stride ld_w, targets [N] int64 in h16's row order (labelled rows first when
+    n_grad < N). Returns token_loss, token_entropy, correct (int32), grad [N, hidden_cols] fp16
+    (rows placed through grad_rows) or None."""
+    lib = _lib.load()
+    device = h16.device
+    n_tokens = h16.shape[0]
+    vocab = w16.shape[0]
+    stream = _lib.stream_of(device)
+    stats = torch.empty(n_tokens, _lib.HEAD_STATS, dtype=torch.float32, device=device)
+    acc = torch.empty(n_grad, hidden_cols, dtype=torch.float32, device=device) if n_grad else None
+    size = _lib._SZ(0)
+    _lib.check(lib.talm_head_workspace_size(n_tokens, n_grad, hidden_cols, vocab, vocab_chunk,
+                                            size), "talm_head_workspace_size")
+    ws = torch.empty(size.value, dtype=torch.uint8, device=device)
+    _lib.check(lib.talm_head_shard(_lib.ptr(h16), h16.stride(0), _lib.ptr(w16), ld_w,
+                                   _lib.ptr(targets), n_tokens, n_grad, hidden_cols, vocab, 0,
+                                   vocab_chunk, _lib.ptr(stats), _lib.ptr(acc), _lib.ptr(ws),
+                                   size.value, stream), "talm_head_shard")
+    token_loss = torch.empty(n_tokens, dtype=torch.float32, device=device)
+    token_entropy = torch.empty_like(token_loss)
+    correct = torch.empty(n_tokens, dtype=torch.int32, device=device)
+    grad = (torch.empty(n_tokens, hidden_cols, dtype=torch.float16, device=device)
+            if want_grad else None)
+    _lib.check(lib.talm_head_finalize(_lib.ptr(stats), _lib.ptr(targets), n_tokens, n_grad,
+                                      _lib.ptr(acc), None, _lib.ptr(w16), ld_w, 0, vocab,
+                                      hidden_cols, _lib.ptr(grad_rows), _lib.ptr(token_loss),
+                                      _lib.ptr(token_entropy), _lib.ptr(correct),
+                                      _lib.ptr(grad), 0, stream), "talm_head_finalize")
+    return token_loss, token_entropy, correct, grad
+
+
+class FusedHeadLossVocab(torch.autograd.Function):
+    """loss, per-token loss, per-token entropy, per-token correctness from hidden states and the
+    frozen output weight, walking the vocabulary in slices (fused_head.py:302-397). Saves only
+    the fp16 hidden gradient. With the gradient on and COMPACT, the rows are put labelled-first
+    so the accumulator GEMM covers the labelled rows only; every output comes back in the input
+    order."""
+
+    @staticmethod
+    def forward(ctx, hidden, weight, targets, num_items, vocab_chunk, need_grad, n_labelled):
+        _check_cuda(hidden, weight, targets)
+        n_tokens, hidden_size = hidden.shape
+        cols = _pad8(hidden_size)
+        h16, _ = _operand(hidden.detach().to(torch.float16), cols)
+        w16, ld_w = _operand(weight.detach(), cols)
+        targets = targets.contiguous().to(torch.int64)
+        labelled = targets >= 0
+
+        n_grad, src, rows_targets = (n_tokens if need_grad else 0), None, targets
+        if need_grad and COMPACT and n_tokens > 0:
+            if n_labelled is None:
+                n_labelled = int(labelled.sum())
+            n_grad = int(n_labelled)
+            if 0 < n_grad < n_tokens:
+                _dest, src = labelled_first(labelled, n_grad)
+                h16 = h16.index_select(0, src)
+                rows_targets = targets.index_select(0, src)
+                RAN["compact"] += 1
+
+        if n_tokens > 0:
+            token_loss, token_entropy, correct, grad = head_forward(
+                h16, w16, ld_w, rows_targets, n_grad, cols, int(vocab_chunk), grad_rows=src,
+                want_grad=need_grad)
+        else:
+            token_loss = torch.empty(0, dtype=torch.float32, device=hidden.device)
+            token_entropy = torch.empty_like(token_loss)
+            correct = torch.empty(0, dtype=torch.int32, device=hidden.device)
+            grad = torch.empty(0, cols, dtype=torch.float16, device=hidden.device)
+        if need_grad and cols != hidden_size:
+            grad = grad[:, :hidden_size]
+
+        denom = _denominator(num_items, labelled.sum())
+        loss = token_loss.sum() / denom
+        correct = correct.to(torch.bool)
+        ctx.denom = denom
+        ctx.out_dtype = hidden.dtype
+        if need_grad:
+            ctx.save_for_backward(grad)
+        ctx.mark_non_differentiable(token_loss, token_entropy, correct)
+        return loss, token_loss, token_entropy, correct
+
+    @staticmethod
+    def backward(ctx, grad_loss, _grad_token_loss, _grad_entropy, _grad_correct):
+        return _head_backward(ctx, grad_loss), None, None, None, None, None, None
+
+
+class FusedHeadLoss(torch.autograd.Function):
+    """Token-chunked entry point (fused_head.py:400-444), same signature. The reference's
+    token-chunked kernel is replaced by the vocabulary-sliced CUDA path (same outputs); `chunk`
+    is accepted and ignored."""
+
+    @staticmethod
+    def forward(ctx, hidden, weight, targets, num_items, chunk, need_grad):
+        outs = FusedHeadLossVocab.forward(ctx, hidden, weight, targets, num_items, VOCAB_CHUNK,
+                                          need_grad, None)
+        return outs
+
+    @staticmethod
+    def backward(ctx, grad_loss, _grad_token_loss, _grad_entropy, _grad_correct):
+        return _head_backward(ctx, grad_loss), None, None, None, None, None
+
+
+def fused_head_loss(hidden, weight, targets, num_items=None, vocab_chunk=None, *,
+                    token_chunk=None, n_labelled=None):
+    """hidden [N, H] (fp16/fp32/bf16, may require grad), weight [V, H] frozen, targets [N] int64
+    already shifted (-100 = ignore). Returns (loss, token_loss[N], token_entropy[N], correct[N])
+    (fused_head.py:447-462). `n_labelled`: the host count of targets >= 0 when the caller has it
+    (saves a host sync); it must be exact."""
+    need_grad = torch.is_grad_enabled() and hidden.requires_grad
+    if token_chunk is None and VOCAB_PATH and weight.dim() == 2 and weight.stride(1) == 1:
+        RAN["vchunk"] += 1
+        return FusedHeadLossVocab.apply(hidden, weight, targets, num_items,
+                                        vocab_chunk or VOCAB_CHUNK, need_grad, n_labelled)
+    if VOCAB_PATH:
+        FELL_BACK["vchunk"] += 1
+    return FusedHeadLoss.apply(hidden, weight, targets, num_items, token_chunk or DEFAULT_CHUNK,
+                               need_grad)

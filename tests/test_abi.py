@@ -1,0 +1,84 @@
+"""The C-ABI library builds, loads and exports every entry point include/talm.h declares; the
+argument checks that run before any CUDA call answer on any machine. No kernel is launched."""
+
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from talm_b200 import _lib, build
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "talm.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(talm_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return _lib.load()
+
+
+def test_header_declares_the_abi():
+    names = declared_functions()
+    assert "talm_nf4_dequantize" in names and "talm_nf4_group_dequant" in names
+    assert "talm_head_shard" in names and "talm_head_finalize" in names
+    assert set(names) <= set(_lib.SIGNATURES), set(names) - set(_lib.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", build.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (talm_\w+)", out))
+    missing = set(declared_functions()) - exported
+    assert not missing, f"declared in talm.h but not exported: {sorted(missing)}"
+    for name in declared_functions():
+        assert getattr(lib, name) is not None
+
+
+def test_no_library_allocates_or_batches_copies():
+    """The C ABI never allocates (callers pass workspace) and never uses batched copies."""
+    csrc = os.path.join(ROOT, "talm_b200", "csrc")
+    for name in os.listdir(csrc):
+        text = open(os.path.join(csrc, name)).read()
+        assert "cudaMalloc" not in text, name
+        assert "Batch" + "Async" not in text, name
+
+
+def test_status_strings_and_version(lib):
+    assert lib.talm_abi_version() == 1
+    assert lib.talm_status_string(0) == b"ok"
+    assert lib.talm_status_string(1) == b"invalid argument"
+
+
+def test_argument_errors_are_reported_before_any_launch(lib):
+    # odd element count and odd block size: rejected on the host
+    assert lib.talm_nf4_dequantize(None, None, 3, 64, None, None) == 1
+    assert b"even" in lib.talm_last_error()
+    assert lib.talm_nf4_dequantize(None, None, 4, 63, None, None) == 1
+    assert lib.talm_nf4_group_dequant(None, None, None, None, None, None, None, 4, 96, 256,
+                                      None) == 1
+    assert lib.talm_nf4_group_dequant(None, None, None, None, None, None, None,
+                                      1 << 26, 64, 256, None) == 3
+    # head: n_grad > n_tokens, odd hidden size
+    assert lib.talm_head_shard(None, 8, None, 8, None, 4, 5, 8, 10, 0, 8, None, None, None, 0,
+                               None) == 1
+    assert lib.talm_head_shard(None, 12, None, 12, None, 4, 2, 12, 10, 0, 8, None, None, None,
+                               0, None) == 1
+    assert lib.talm_head_combine(None, 2, 4, 2, 0, None, None, None) == 1
+    # zero-sized work is a no-op
+    assert lib.talm_nf4_dequantize(None, None, 0, 64, None, None) == 0
+
+
+def test_workspace_size_is_host_only(lib):
+    size = ctypes.c_size_t(0)
+    assert lib.talm_head_workspace_size(2048, 1126, 1536, 151936, 8192, ctypes.byref(size)) == 0
+    # P slice (n_grad x chunk fp16) dominates: 1126 * 8192 * 2 bytes
+    assert 1126 * 8192 * 2 < size.value < 1126 * 8192 * 2 + 4 * 2**20
