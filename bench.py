@@ -1,0 +1,557 @@
+#!/usr/bin/env python
+"""Benchmark of the two hot paths on B200, one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1: one rank per GPU, NCCL)
+
+Headline (`value`): fused LM head + cross-entropy, forward + backward, tokens/s over all GPUs on
+BASELINE config 4 - hidden [16384, 1536] fp16 N(0,1), weight [151936, 1536] fp16 N(0,0.02),
+labels uniform over the vocabulary, no pad - with the vocabulary sharded over the N GPUs
+(strong scaling; at N=1 the whole vocabulary on one GPU). A step is one call of the public API
+(`fused_head_loss` at N=1, `vocab_parallel_head_loss` at N>1) plus `loss.backward()`, inputs
+resident in HBM. The weight (467 MB) is larger than L2, so no flush is needed between steps.
+
+Same line, secondary objects:
+  c2   BASELINE config 2 on one GPU (hidden [2048, 1536], ~45% trailing pad, N=1 only)
+  nf4  config 1 (one Qwen2.5-1.5B layer, fp32 absmax, N=1 only) and config 3 (28 layers,
+       double-quantised absmax, one grouped launch per layer, layers sharded over the ranks)
+  e2e  the headline through the same API with host buffers: pinned-host -> device copies of the
+       step's hidden states and labels and the device -> host read of the loss inside the timed
+       region
+  roofline     the dominant kernel (head_logits_kernel) against the measured bf16/fp16 peak
+  cpu_baseline the CPU oracle (a restatement of the reference's torch formula,
+               solution/test_kernels.py:70-83) on a bounded sample, rank 0, N=1
+
+`--impl reference` times the reference's CPU formula (the oracle port) on the box's host cores
+on a bounded sample per step and prints the same metric with "impl": "reference"; under
+torchrun only rank 0 runs it.
+"""
+
+import argparse
+import datetime
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+VOCAB, HIDDEN = 151936, 1536
+C4_TOKENS = 16384
+C2_TOKENS = 2048
+CHUNK = 8192
+QWEN_SHAPES = [(1536, 1536), (256, 1536), (256, 1536), (1536, 1536), (8960, 1536),
+               (8960, 1536), (1536, 8960)]
+N_LAYERS = 28
+METRIC = "fused LM-head+CE fwd+bwd tokens/s (vocab-parallel, config 4) & NF4 dequant GB/s"
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--no-secondary", action="store_true",
+                   help="headline only (no c2 / nf4 / cpu baseline)")
+    return p.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d["bf16_tflops_sustained"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def profile_traffic(name):
+    """Per-launch DRAM bytes of a kernel from the committed ncu summary (profiles/<name>.md,
+    a line `traffic_bytes_per_launch: <int>`), or None."""
+    path = os.path.join(ROOT, "profiles", name + ".md")
+    if not os.path.exists(path):
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", open(path).read())
+    return int(m.group(1)) if m else None
+
+
+# ------------------------------------------------------------------------------------------
+# process group and timing
+# ------------------------------------------------------------------------------------------
+def init_dist(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(value, world):
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def timed(fn, steps, world):
+    """Device time of `steps` calls of fn (CUDA events on the current stream, barrier and
+    synchronize on both sides), max over ranks, in ms."""
+    barrier(world)
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    stop.record()
+    barrier(world)
+    return max_over_ranks(start.elapsed_time(stop), world)
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during a timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, enabled):
+        self.proc = None
+        self.path = None
+        if not enabled:
+            return
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.out, stderr=subprocess.DEVNULL)
+        except Exception:  # noqa: BLE001 - no nvidia-smi: no clock record
+            self.proc = None
+
+    def stop(self, gpus):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        self.out.close()
+        sm, smax, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) not in gpus:
+                continue
+            try:
+                clk, mx = float(parts[1]), float(parts[2])
+            except ValueError:
+                continue
+            smax = max(smax, mx)
+            sm.append(clk)
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        loaded = [c for c in sm if c > 0.5 * smax] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------
+# synthetic inputs (seeded; the shapes and distributions of BASELINE.json's configs)
+# ------------------------------------------------------------------------------------------
+def gen(seed, device="cuda"):
+    return torch.Generator(device=device).manual_seed(seed)
+
+
+def head_weight(device):
+    return (torch.randn(VOCAB, HIDDEN, generator=gen(1, device), device=device) * 0.02).half()
+
+
+def c4_inputs(device):
+    hidden = torch.randn(C4_TOKENS, HIDDEN, generator=gen(2, device), device=device).half()
+    targets = torch.randint(0, VOCAB, (C4_TOKENS,), generator=gen(3, device), device=device)
+    return hidden, targets
+
+
+def c2_inputs(device):
+    """Batch 4 x seq 512, ~45% trailing pad per row (pad lengths seeded), labels -100 there."""
+    hidden = torch.randn(C2_TOKENS, HIDDEN, generator=gen(4, device), device=device).half()
+    targets = torch.randint(0, VOCAB, (C2_TOKENS,), generator=gen(5, device), device=device)
+    rng = np.random.default_rng(6)
+    pads = rng.integers(int(0.35 * 512), int(0.55 * 512), size=4)
+    pads[-1] = max(0, int(round(0.45 * C2_TOKENS)) - int(pads[:-1].sum()))
+    for row, pad in enumerate(pads):
+        if pad:
+            targets[row * 512 + 512 - int(pad): row * 512 + 512] = -100
+    return hidden, targets
+
+
+def nf4_layer(seed, device, double_quant):
+    g = gen(100 + seed, device)
+    n = sum(o * i for o, i in QWEN_SHAPES)
+    packed = torch.randint(0, 256, (n // 2,), generator=g, device=device, dtype=torch.uint8)
+    out = torch.empty(n, dtype=torch.float16, device=device)
+    if not double_quant:
+        absmax = torch.rand(n // 64, generator=g, device=device) * 0.19 + 0.01
+        return {"packed": packed, "absmax": absmax, "out": out, "n": n}
+    absmax8 = torch.randint(0, 256, (n // 64,), generator=g, device=device, dtype=torch.uint8)
+    code = torch.sort(torch.rand(256, generator=g, device=device) * 2 - 1).values
+    absmax2 = torch.rand(n // (64 * 256), generator=g, device=device) * 0.19 + 0.01
+    offsets = []
+    for o, i in QWEN_SHAPES:
+        offsets.append(torch.full((o * i // (64 * 256),), float(0.01 + 0.005 * len(offsets)),
+                                  device=device))
+    return {"packed": packed, "absmax8": absmax8, "code": code, "absmax2": absmax2,
+            "offset2": torch.cat(offsets), "out": out, "n": n}
+
+
+# ------------------------------------------------------------------------------------------
+# our arm
+# ------------------------------------------------------------------------------------------
+def head_step_fn(world, rank, hidden, weight, targets, n_labelled):
+    from talm_b200.fused_head import fused_head_loss
+    from talm_b200.vocab_parallel import vocab_parallel_head_loss
+
+    x = hidden.detach().requires_grad_(True)
+    col0 = 0
+    if world > 1:
+        from talm_b200.vocab_parallel import shard_bounds
+
+        col0, _ = shard_bounds(VOCAB, world, rank)
+
+    def step(h=x, t=targets):
+        h.grad = None
+        if world == 1:
+            loss, *_ = fused_head_loss(h, weight, t, None, CHUNK, n_labelled=n_labelled)
+        else:
+            loss, *_ = vocab_parallel_head_loss(h, weight, t, VOCAB, col0, None, CHUNK,
+                                                n_labelled=n_labelled)
+        loss.backward()
+        return loss
+
+    return step
+
+
+def head_flops(n_tokens, n_labelled, vocab=VOCAB):
+    """Algorithmic FLOPs of one head step: logits GEMM over every row + dH GEMM over the
+    labelled rows (2 H V (N + N_lab))."""
+    return 2 * HIDDEN * vocab * (n_tokens + n_labelled)
+
+
+def profile_kernels(fn, steps):
+    from talm_b200 import _lib
+
+    torch.cuda.synchronize()
+    _lib.profile_begin()
+    for _ in range(steps):
+        fn()
+    torch.cuda.synchronize()
+    return _lib.profile_end()
+
+
+def run_head(world, rank, local, steps, warmup, hidden, weight, targets, clocks_on):
+    n_tokens = hidden.shape[0]
+    n_lab = int((targets >= 0).sum())
+    step = head_step_fn(world, rank, hidden, weight, targets, n_lab)
+    for _ in range(warmup):
+        step()
+    sampler = ClockSampler(clocks_on and rank == 0)
+    ms = timed(step, steps, world)
+    clocks = sampler.stop(set(range(world))) if rank == 0 else None
+    prof = profile_kernels(step, steps)
+    return {"ms_per_step": ms / steps, "n_tokens": n_tokens, "n_labelled": n_lab,
+            "clocks": clocks, "kernels": prof}
+
+
+def run_head_e2e(world, rank, steps, warmup, hidden, weight, targets):
+    """Public API with host buffers: H2D of the step's hidden states + labels, D2H of the loss."""
+    from talm_b200.fused_head import fused_head_loss
+    from talm_b200.vocab_parallel import shard_bounds, vocab_parallel_head_loss
+
+    h_host = hidden.cpu().pin_memory()
+    t_host = targets.cpu().pin_memory()
+    n_lab = int((t_host >= 0).sum())
+    col0 = shard_bounds(VOCAB, world, rank)[0] if world > 1 else 0
+    sink = []
+
+    def step():
+        h = h_host.to("cuda", non_blocking=True).requires_grad_(True)
+        t = t_host.to("cuda", non_blocking=True)
+        if world == 1:
+            loss, *_ = fused_head_loss(h, weight, t, None, CHUNK, n_labelled=n_lab)
+        else:
+            loss, *_ = vocab_parallel_head_loss(h, weight, t, VOCAB, col0, None, CHUNK,
+                                                n_labelled=n_lab)
+        loss.backward()
+        sink.append(loss.item())
+
+    for _ in range(warmup):
+        step()
+    ms = timed(step, steps, world)
+    h2d = (h_host.numel() * h_host.element_size() + t_host.numel() * 8) * world
+    return ms / steps, h2d, 4 * world
+
+
+def run_nf4(world, rank, steps, warmup):
+    """Config 3 (28 layers, double-quantised, layer-sharded) and, on one GPU, config 1."""
+    from talm_b200 import _lib
+    from talm_b200.nf4_dequant import nf4_dequantize
+    from talm_b200.qgroup import launch, _levels
+    from talm_b200.vocab_parallel import shard_bounds
+
+    res = {}
+    l0, nl = shard_bounds(N_LAYERS, world, rank)
+    layers = [nf4_layer(l0 + i, "cuda", True) for i in range(nl)]
+    levels = _levels(torch.device("cuda"))
+    n_rows = layers[0]["n"] // 64 if layers else 0
+
+    def sweep():
+        for L in layers:
+            launch(L["packed"], L["absmax8"], L["code"], L["absmax2"], L["offset2"], levels,
+                   L["out"], n_rows, 64, 256)
+
+    for _ in range(warmup):
+        sweep()
+    ms = timed(sweep, steps, world)
+    prof = profile_kernels(sweep, steps)
+    total_bytes = N_LAYERS * 117_736_832
+    k_ms, k_n = prof["nf4"]
+    res["c3"] = {"workload": "28 Qwen2.5-1.5B layers, double-quantised absmax, one grouped "
+                             "launch per layer, layers sharded contiguously over the ranks",
+                 "GB_per_s": total_bytes / (ms / steps) / 1e6, "ms_per_sweep": ms / steps,
+                 "bytes_per_sweep": total_bytes,
+                 "kernel_us_per_layer": 1000 * k_ms / max(k_n, 1)}
+    del layers
+    if world == 1:
+        # config 1: fp32 absmax, one launch per layer over its concatenated buffers; eight
+        # distinct layers in rotation (0.96 GB) so no launch finds its data in L2
+        c1 = [nf4_layer(200 + i, "cuda", False) for i in range(8)]
+        it = {"i": 0}
+
+        def one():
+            L = c1[it["i"] % len(c1)]
+            it["i"] += 1
+            nf4_dequantize(L["packed"], L["absmax"], 64, L["out"])
+
+        for _ in range(warmup * 8):
+            one()
+        n = steps * 8
+        ms = timed(one, n, 1)
+        prof = profile_kernels(one, n)
+        k_ms, k_n = prof["nf4"]
+        per = 119_906_368
+        res["c1"] = {"workload": "one Qwen2.5-1.5B layer (46,792,704 weights), fp32 absmax, "
+                                 "blocksize 64",
+                     "GB_per_s": per / (ms / n) / 1e6, "us_per_layer": 1000 * ms / n,
+                     "kernel_GB_per_s": per / (k_ms / max(k_n, 1)) / 1e6,
+                     "bytes_per_layer": per}
+        del c1
+    torch.cuda.empty_cache()
+    _ = _lib
+    return res
+
+
+def cpu_head_baseline(weight, hidden, targets, budget_s=12.0):
+    """The oracle (torch CPU restatement of the reference's head formula) on a bounded sample of
+    the workload's rows against the full vocabulary; tokens/s."""
+    from oracle.head import reference_head
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    w = weight.cpu()
+    h = hidden.cpu()
+    t = targets.cpu()
+    n = 4
+    t0 = time.perf_counter()
+    reference_head(h[:n], w, t[:n])
+    dt = time.perf_counter() - t0
+    n = int(max(4, min(hidden.shape[0], n * budget_s / max(dt, 1e-3))))
+    t0 = time.perf_counter()
+    reference_head(h[:n], w, t[:n])
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "tokens/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"{n} rows of the workload x full vocabulary "
+                                      f"({VOCAB}) x hidden {HIDDEN}, forward + dH, {dt:.1f} s"}
+
+
+def ours(args, world, rank, local):
+    pk = peaks()
+    weight_full = head_weight("cuda")
+    hidden, targets = c4_inputs("cuda")
+    if world > 1:
+        from talm_b200.vocab_parallel import shard_bounds
+
+        col0, cols = shard_bounds(VOCAB, world, rank)
+        weight = weight_full[col0:col0 + cols].contiguous()
+        del weight_full
+        torch.cuda.empty_cache()
+    else:
+        weight = weight_full
+    head = run_head(world, rank, local, args.steps, args.warmup, hidden, weight, targets, True)
+    e2e_ms, h2d, d2h = run_head_e2e(world, rank, args.steps, args.warmup, hidden, weight,
+                                    targets)
+    n_tok, n_lab = head["n_tokens"], head["n_labelled"]
+    value = n_tok / (head["ms_per_step"] / 1000)
+
+    kernels = head["kernels"]
+    total_ms = sum(v[0] for v in kernels.values()) or 1.0
+    lg_ms, lg_n = kernels["head_logits"]
+    cols_rank = weight.shape[0]
+    # algorithmic FLOPs of one logits launch: 2 H x (slice columns) x N; slices of CHUNK
+    n_slices = -(-cols_rank // CHUNK)
+    logits_flops = 2 * HIDDEN * cols_rank * n_tok / n_slices
+    ach = logits_flops / (lg_ms / max(lg_n, 1) / 1000) / 1e12 if lg_n else None
+    acc_ms, acc_n = kernels["head_accum"]
+    acc_flops = 2 * HIDDEN * cols_rank * n_lab / n_slices
+    acc_ach = acc_flops / (acc_ms / max(acc_n, 1) / 1000) / 1e12 if acc_n else None
+    peak = pk["bf16_tflops_sustained"]
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": head["ms_per_step"],
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "fp16",
+        "data": "synthetic, seeded (shapes and distributions of BASELINE.json configs 1-4)",
+        "config": {"workload": "config 4: fused LM head + CE fwd+bwd, hidden [16384,1536] fp16 "
+                               "N(0,1), weight [151936,1536] fp16 N(0,0.02), all rows labelled, "
+                               f"vocab_chunk {CHUNK}, vocabulary sharded over {world} GPU(s)",
+                   "global_batch": n_tok, "seq_len": n_tok, "hidden": HIDDEN, "vocab": VOCAB,
+                   "parallelism": f"vocab{world}",
+                   "l2": "inputs larger than L2 (weight 467 MB), no flush"},
+        "roofline": {"bound": "tensor", "kernel": "head_logits_kernel",
+                     "achieved": ach, "peak": peak, "unit": "TFLOP/s",
+                     "frac": (ach / peak) if ach else None,
+                     "peak_source": f"{pk['source']} bf16 sustained (kernel inside a long step)",
+                     "frac_of_burst": (ach / pk["bf16_tflops"]) if ach else None,
+                     "traffic": profile_traffic("head_logits_c4"),
+                     "flops_per_launch": logits_flops,
+                     "accum_kernel_TFLOPs": acc_ach,
+                     "step_TFLOPs": head_flops(n_tok, n_lab) / (head["ms_per_step"] / 1000)
+                     / 1e12},
+        "e2e": {"value": n_tok / (e2e_ms / 1000), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": int(sum(v[1] for v in kernels.values()) / max(args.steps, 1)
+                            * args.steps * world),
+        "clocks": head["clocks"],
+        "kernels": {k: {"ms_per_step": v[0] / args.steps, "launches_per_step": v[1] / args.steps,
+                        "share": v[0] / total_ms} for k, v in kernels.items() if v[1]},
+    }
+    del hidden
+    if not args.no_secondary:
+        if world == 1:
+            h2, t2 = c2_inputs("cuda")
+            c2 = run_head(1, 0, 0, args.steps, args.warmup, h2, weight, t2, False)
+            k2 = c2["kernels"]
+            line["c2"] = {"workload": "config 2: hidden [2048,1536], ~45% trailing pad, one GPU",
+                          "tokens_per_s": C2_TOKENS / (c2["ms_per_step"] / 1000),
+                          "ms_per_step": c2["ms_per_step"], "n_labelled": c2["n_labelled"],
+                          "step_TFLOPs": head_flops(C2_TOKENS, c2["n_labelled"])
+                          / (c2["ms_per_step"] / 1000) / 1e12,
+                          "step_frac_of_peak": head_flops(C2_TOKENS, c2["n_labelled"])
+                          / (c2["ms_per_step"] / 1000) / 1e12 / pk["bf16_tflops"],
+                          "kernels_ms_per_step": {k: v[0] / args.steps for k, v in k2.items()
+                                                  if v[1]}}
+        nf4 = run_nf4(world, rank, args.steps, args.warmup)
+        if "c1" in nf4:
+            nf4["c1"]["roofline"] = {"bound": "hbm", "achieved": nf4["c1"]["kernel_GB_per_s"],
+                                     "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                     "frac": nf4["c1"]["kernel_GB_per_s"] / pk["hbm_gbs"],
+                                     "traffic": profile_traffic("nf4_c1_layer")}
+        nf4["c3"]["frac_of_hbm_per_gpu"] = nf4["c3"]["GB_per_s"] / world / pk["hbm_gbs"]
+        line["nf4"] = nf4
+        if world == 1 and rank == 0:
+            line["cpu_baseline"] = cpu_head_baseline(weight, c4_inputs("cuda")[0],
+                                                     c4_inputs("cuda")[1])
+    return line
+
+
+def reference(args, world, rank):
+    """--impl reference: the reference's head formula on the CPU (oracle port), rank 0 only."""
+    if rank != 0:
+        return None
+    from oracle.head import reference_head
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    w = head_weight("cpu") if not torch.cuda.is_available() else head_weight("cuda").cpu()
+    hidden, targets = c4_inputs("cuda") if torch.cuda.is_available() else c4_inputs("cpu")
+    hidden, targets = hidden.cpu(), targets.cpu()
+    n = 8
+    times = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        reference_head(hidden[:n], w, targets[:n])
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    per_step = sum(times) / len(times)
+    value = n / per_step
+    return {"metric": METRIC, "impl": "reference", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": per_step * 1000, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp32 (fp16-rounded logits)", "data": "synthetic",
+            "config": {"workload": "config 4 rows (bounded sample) x full vocabulary on CPU",
+                       "global_batch": n, "seq_len": n, "parallelism": "cpu"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s",
+                             "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": f"{n} rows of config 4 per step x vocab {VOCAB} x "
+                                       f"hidden {HIDDEN}, forward + dH"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            line = reference(args, world, rank)
+            print(json.dumps(line), flush=True)
+        return
+    world, rank, local = init_dist(args.gpus)
+    try:
+        line = ours(args, world, rank, local)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -47,6 +47,23 @@ const char* talm_status_string(int status);
  * reference counterpart: the reference's Triton kernels have no device-side waits. */
 int talm_device_status(int* status_out);
 
+/* Kernel-level timing (the counterpart of the reference's Triton launch timer,
+ * harness/_train.py:44-85): between talm_profile_begin and talm_profile_end every kernel this
+ * library launches is bracketed by CUDA events on its own stream. talm_profile_end synchronises
+ * on those events and returns, per kernel kind, the summed device milliseconds and the launch
+ * count (arrays of n_kinds entries, n_kinds <= TALM_KERNEL_KINDS). Off by default; when off the
+ * launches carry no events. Not thread-safe: profile from one host thread. */
+#define TALM_KERNEL_HEAD_LOGITS 0   /* head_logits_kernel   (tcgen05 logits GEMM + stats) */
+#define TALM_KERNEL_HEAD_COMBINE 1  /* head_combine_kernel  (per-slice merge)             */
+#define TALM_KERNEL_HEAD_ACCUM 2    /* head_accum_kernel    (tcgen05 accumulator GEMM)    */
+#define TALM_KERNEL_HEAD_FINALIZE 3 /* head_finalize_kernel                               */
+#define TALM_KERNEL_HEAD_MERGE 4    /* head_merge_shards_kernel                           */
+#define TALM_KERNEL_NF4 5           /* nf4 chunk kernel (16-byte vectorised main body)    */
+#define TALM_KERNEL_NF4_TAIL 6      /* nf4 byte kernel (tails, unaligned pointers)        */
+#define TALM_KERNEL_KINDS 7
+int talm_profile_begin(void);
+int talm_profile_end(double* ms_out, int64_t* launches_out, int n_kinds);
+
 /* ------------------------------------------------------------------------------------------
  * NF4 dequantisation
  * ---------------------------------------------------------------------------------------- */

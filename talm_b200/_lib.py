@@ -24,6 +24,8 @@ SIGNATURES = {
     "talm_last_error": (ctypes.c_char_p, []),
     "talm_status_string": (ctypes.c_char_p, [_INT]),
     "talm_device_status": (_INT, [ctypes.POINTER(_INT)]),
+    "talm_profile_begin": (_INT, []),
+    "talm_profile_end": (_INT, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_I64), _INT]),
     "talm_nf4_dequantize": (_INT, [_P, _P, _I64, _I64, _P, _P]),
     "talm_nf4_group_dequant": (_INT, [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     "talm_head_workspace_size": (_INT, [_I64, _I64, _I64, _I64, _I64, ctypes.POINTER(_SZ)]),
@@ -79,6 +81,23 @@ def ptr(t):
 
 def stream_of(device):
     return torch.cuda.current_stream(device).cuda_stream
+
+
+KERNEL_KINDS = ("head_logits", "head_combine", "head_accum", "head_finalize", "head_merge",
+                "nf4", "nf4_tail")
+
+
+def profile_begin():
+    check(load().talm_profile_begin(), "talm_profile_begin")
+
+
+def profile_end():
+    """{kind: (total device ms, launches)} of the kernels launched since profile_begin."""
+    n = len(KERNEL_KINDS)
+    ms = (ctypes.c_double * n)()
+    cnt = (_I64 * n)()
+    check(load().talm_profile_end(ms, cnt, n), "talm_profile_end")
+    return {k: (ms[i], cnt[i]) for i, k in enumerate(KERNEL_KINDS)}
 
 
 def device_status():

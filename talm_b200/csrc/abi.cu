@@ -5,6 +5,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <vector>
+
 #include "common.cuh"
 
 namespace talm {
@@ -42,6 +44,34 @@ bool device_is_sm100() {
   if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
     return false;
   return major == 10 && minor == 0;
+}
+
+struct ProfileRecord {
+  int kind;
+  cudaEvent_t start, stop;
+};
+static bool g_profile_on = false;
+static std::vector<ProfileRecord> g_profile;
+
+LaunchTimer::LaunchTimer(int kind, cudaStream_t stream)
+    : kind_(kind), stream_(stream), start_(nullptr) {
+  if (!g_profile_on) return;
+  cudaEvent_t e;
+  if (cudaEventCreate(&e) == cudaSuccess) {
+    cudaEventRecord(e, stream);
+    start_ = e;
+  }
+}
+
+LaunchTimer::~LaunchTimer() {
+  if (start_ == nullptr) return;
+  cudaEvent_t e;
+  if (cudaEventCreate(&e) != cudaSuccess) {
+    cudaEventDestroy(static_cast<cudaEvent_t>(start_));
+    return;
+  }
+  cudaEventRecord(e, stream_);
+  g_profile.push_back({kind_, static_cast<cudaEvent_t>(start_), e});
 }
 
 }  // namespace talm
@@ -103,6 +133,42 @@ const char* talm_status_string(int status) {
     case TALM_ETIMEOUT: return "device-side wait timed out";
     default: return "unknown status";
   }
+}
+
+int talm_profile_begin(void) {
+  for (auto& r : talm::g_profile) {
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  talm::g_profile.clear();
+  talm::g_profile_on = true;
+  return TALM_OK;
+}
+
+int talm_profile_end(double* ms_out, int64_t* launches_out, int n_kinds) {
+  talm::g_profile_on = false;
+  if (n_kinds < 0 || n_kinds > TALM_KERNEL_KINDS || (n_kinds > 0 && (!ms_out || !launches_out)))
+    return talm::set_error(TALM_EINVAL, "bad profile output arrays");
+  for (int k = 0; k < n_kinds; ++k) {
+    ms_out[k] = 0.0;
+    launches_out[k] = 0;
+  }
+  int status = TALM_OK;
+  for (auto& r : talm::g_profile) {
+    float ms = 0.0f;
+    if (cudaEventSynchronize(r.stop) != cudaSuccess ||
+        cudaEventElapsedTime(&ms, r.start, r.stop) != cudaSuccess) {
+      status = talm::set_error(TALM_ECUDA, "profile event: %s",
+                               cudaGetErrorString(cudaGetLastError()));
+    } else if (r.kind >= 0 && r.kind < n_kinds) {
+      ms_out[r.kind] += ms;
+      launches_out[r.kind] += 1;
+    }
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  talm::g_profile.clear();
+  return status;
 }
 
 int talm_device_status(int* status_out) {

@@ -20,6 +20,16 @@ int check_launch(const char* what);
 int current_sm_count();
 bool device_is_sm100();
 
+// Launch timing (talm_profile_begin / talm_profile_end): a scope around one kernel launch that
+// records CUDA events on the launch stream while profiling is on, and does nothing otherwise.
+struct LaunchTimer {
+  LaunchTimer(int kind, cudaStream_t stream);
+  ~LaunchTimer();
+  int kind_;
+  cudaStream_t stream_;
+  void* start_;
+};
+
 // Device status word set by bounded waits that gave up (read by talm_device_status). The
 // library is built as one translation unit (talm.cu), so this header is seen once.
 __device__ int g_device_status = 0;

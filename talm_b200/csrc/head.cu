@@ -776,13 +776,19 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
     lp.ldp = chunk;
     lp.stats = stats;
     const int tiles = n_row_tiles * n_col_tiles;
+    {
+    LaunchTimer timer(TALM_KERNEL_HEAD_LOGITS, stream);
     head_logits_kernel<<<tiles < sms ? tiles : sms, 192, SMEM_BYTES, stream>>>(tm_hidden,
                                                                              tm_weight, lp);
+    }
     if ((st = check_launch("head logits kernel")) != TALM_OK) return st;
 
+    {
+    LaunchTimer timer(TALM_KERNEL_HEAD_COMBINE, stream);
     head_combine_kernel<<<static_cast<int>((n_tokens + 7) / 8), 256, 0, stream>>>(
         ws.partial, n_col_tiles, static_cast<int>(n_tokens), static_cast<int>(n_grad), s0 == 0,
         stats, ws.tile_scale, ws.alpha);
+    }
     if ((st = check_launch("head combine kernel")) != TALM_OK) return st;
 
     if (n_grad > 0) {
@@ -799,6 +805,7 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
       ap.alpha = ws.alpha;
       ap.acc = acc;
       const int atiles = ap.n_row_tiles * ap.n_h_tiles;
+      LaunchTimer timer(TALM_KERNEL_HEAD_ACCUM, stream);
       head_accum_kernel<<<atiles < sms ? atiles : sms, 320, SMEM_BYTES, stream>>>(
           tm_probs, tm_weight_mn, ap);
       if ((st = check_launch("head accumulator kernel")) != TALM_OK) return st;
@@ -820,6 +827,7 @@ int talm_head_finalize(const float* stats, const int64_t* targets, int64_t n_tok
   if (!stats || !targets) return set_error(TALM_EINVAL, "null pointer");
   if (grad != nullptr && n_grad > 0 && (acc == nullptr || weight == nullptr))
     return set_error(TALM_EINVAL, "gradient needs acc and weight");
+  LaunchTimer timer(TALM_KERNEL_HEAD_FINALIZE, static_cast<cudaStream_t>(stream));
   head::head_finalize_kernel<<<static_cast<int>((n_tokens + 7) / 8), 256, 0,
                                static_cast<cudaStream_t>(stream)>>>(
       stats, reinterpret_cast<const long long*>(targets), static_cast<int>(n_tokens),
@@ -838,6 +846,7 @@ int talm_head_combine(const float* gathered, int64_t n_shards, int64_t n_tokens,
     return set_error(TALM_EINVAL, "bad shard arguments");
   if (n_tokens == 0) return TALM_OK;
   if (!gathered || !stats_out) return set_error(TALM_EINVAL, "null pointer");
+  LaunchTimer timer(TALM_KERNEL_HEAD_MERGE, static_cast<cudaStream_t>(stream));
   head::head_merge_shards_kernel<<<static_cast<int>((n_tokens + 255) / 256), 256, 0,
                                    static_cast<cudaStream_t>(stream)>>>(
       gathered, static_cast<int>(n_shards), static_cast<int>(n_tokens), static_cast<int>(rank),

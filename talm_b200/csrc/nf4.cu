@@ -153,6 +153,7 @@ int run_nf4(const uint8_t* packed, uint16_t* out, int64_t n_elems, int64_t block
       const int64_t want = (n_chunks + 7) / 8;  // 8 warps per block
       const int grid = static_cast<int>(want < int64_t{sms} * 8 ? want : int64_t{sms} * 8);
       uint32_t* pairs = reinterpret_cast<uint32_t*>(out);
+      LaunchTimer timer(TALM_KERNEL_NF4, stream);
       if (blocksize >= 64) {
         nf4_chunks_kernel<Scale, true><<<grid, 256, 0, stream>>>(
             packed, pairs, n_chunks, n_blocks, shift, blocksize, scale, levels);
@@ -169,6 +170,7 @@ int run_nf4(const uint8_t* packed, uint16_t* out, int64_t n_elems, int64_t block
     const int64_t rest = n_bytes - done;
     const int64_t want = (rest + 255) / 256;
     const int grid = static_cast<int>(want < int64_t{sms} * 8 ? want : int64_t{sms} * 8);
+    LaunchTimer timer(TALM_KERNEL_NF4_TAIL, stream);
     nf4_bytes_kernel<Scale><<<grid, 256, 0, stream>>>(
         packed, reinterpret_cast<__half*>(out), done, n_bytes, blocksize, scale, levels);
     int st = check_launch("nf4 byte kernel");
