@@ -64,6 +64,8 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-secondary", action="store_true",
                    help="headline only (no c2 / nf4 / cpu baseline)")
+    p.add_argument("--only-nf4", action="store_true",
+                   help="the NF4 part alone (profiling runs); prints its JSON object")
     return p.parse_args()
 
 
@@ -544,7 +546,10 @@ def main():
         return
     world, rank, local = init_dist(args.gpus)
     try:
-        line = ours(args, world, rank, local)
+        if args.only_nf4:
+            line = {"nf4": run_nf4(world, rank, args.steps, args.warmup)}
+        else:
+            line = ours(args, world, rank, local)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

@@ -104,16 +104,19 @@ int talm_nf4_group_dequant(const uint8_t* packed, const uint8_t* absmax8, const 
 /* Per-row statistics, one float[TALM_HEAD_STATS] record per token row, relative to the part of
  * the vocabulary a call covered (all of it on one GPU, the rank's shard under vocabulary
  * parallelism). Argmax and the target logit are over fp16-rounded logits, as the reference's
- * cuBLAS fp16 GEMM output (solution/fused_head.py:136-169). */
+ * cuBLAS fp16 GEMM output (solution/fused_head.py:136-169). The sums S and T and the
+ * accumulator are kept relative to a per-row reference REF that trails the running max M by at
+ * most 8 (REF <= M <= REF + 8): the reference moves only when the max outgrows it, so most
+ * slices need no rescaling of the probabilities or of the accumulator. */
 #define TALM_HEAD_STATS 8
 #define TALM_STAT_M 0      /* running max of z                                      */
-#define TALM_STAT_S 1      /* sum exp(z - m)                                         */
-#define TALM_STAT_T 2      /* sum exp(z - m) * z                                     */
+#define TALM_STAT_S 1      /* sum exp(z - REF)                                       */
+#define TALM_STAT_T 2      /* sum exp(z - REF) * z                                   */
 #define TALM_STAT_ZT 3     /* z[target] if the target column is covered, else 0       */
-#define TALM_STAT_BEST 4   /* max z (same as m, kept for the argmax key)               */
+#define TALM_STAT_BEST 4   /* max z (same as M, kept for the argmax key)               */
 #define TALM_STAT_IDX 5    /* first global column attaining BEST, as int32 bits        */
 #define TALM_STAT_HIT 6    /* 1.0 if the target column is covered by the call, else 0  */
-#define TALM_STAT_PAD 7
+#define TALM_STAT_REF 7    /* reference of S, T and the accumulator                    */
 
 /* Device bytes of workspace talm_head_shard needs. */
 int talm_head_workspace_size(int64_t n_tokens, int64_t n_grad, int64_t hidden,
@@ -121,7 +124,7 @@ int talm_head_workspace_size(int64_t n_tokens, int64_t n_grad, int64_t hidden,
 
 /* Logits GEMM + online log-sum-exp / entropy numerator / argmax / target logit over the
  * vocabulary columns [vocab_col0, vocab_col0 + vocab_cols) of the weight, in slices of
- * vocab_chunk columns, and (n_grad > 0) the accumulator acc[i] = sum_v exp(z_iv - m_i) W[v]
+ * vocab_chunk columns, and (n_grad > 0) the accumulator acc[i] = sum_v exp(z_iv - REF_i) W[v]
  * of the first n_grad rows (the labelled rows, placed first by the caller).
  * Replaces the slice loop of solution/fused_head.py:356-371 (`torch.mm` logits GEMM,
  * `fused_head_vocab_kernel` stats mode :126-182, `torch.addmm` accumulator GEMM).
@@ -145,8 +148,8 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
  * whole vocabulary, or the combination of all shards).
  * Replaces the last-slice branch of `fused_head_vocab_kernel` (fused_head.py:160-169) and its
  * finalize mode (fused_head.py:111-125).
- *   token_loss[i]    = labelled ? log(s) + m - zt : 0
- *   token_entropy[i] = m + log(s) - t / s
+ *   token_loss[i]    = labelled ? REF + log(S) - zt : 0
+ *   token_entropy[i] = REF + log(S) - T / S
  *   correct[i]       = labelled && idx == target
  *   grad ([n_tokens, hidden], fp16, or fp32 when grad_is_f32 != 0; skipped when NULL):
  *     grad[i] = labelled && i < n_grad ? acc[i] * acc_scale[i] - fp16(W[target_i]) : 0
@@ -165,7 +168,7 @@ int talm_head_finalize(const float* stats, const int64_t* targets, int64_t n_tok
 
 /* Merges the statistics of n_shards vocabulary shards (gathered as [n_shards, n_tokens,
  * TALM_HEAD_STATS], shard r covering the columns of rank r) into one record per row, and
- * writes acc_scale[i] = exp(m_rank - M) / S for this rank's accumulator rows (n_grad rows).
+ * writes acc_scale[i] = exp(REF_rank - REF) / S for this rank's accumulator rows (n_grad rows).
  * No reference counterpart: the reference is single-GPU; this is the exchange step of the
  * vocabulary-parallel head (log-sum-exp merge of online-softmax partials). */
 int talm_head_combine(const float* gathered, int64_t n_shards, int64_t n_tokens, int64_t rank,

@@ -154,6 +154,7 @@ class CpuHeadOps:
         stats[:, 4] = st["m"].float()
         stats[:, 5] = st["idx"].to(torch.int32).view(torch.float32)
         stats[:, 6] = st["hit"].float()
+        stats[:, 7] = st["m"].float()        # reference of s, t and acc: the max itself
         acc = None
         if n_grad:
             acc = torch.zeros(n_grad, hidden_cols, dtype=torch.float64)
@@ -167,8 +168,9 @@ class CpuHeadOps:
 
     def combine(self, gathered, rank, n_grad):
         m = gathered[:, :, 0].double()
-        big = m.max(0).values
-        w = torch.exp(m - big)
+        ref = gathered[:, :, 7].double()
+        big = ref.max(0).values
+        w = torch.exp(ref - big)
         s = (gathered[:, :, 1].double() * w).sum(0)
         t = (gathered[:, :, 2].double() * w).sum(0)
         best = gathered[:, :, 4]
@@ -179,7 +181,8 @@ class CpuHeadOps:
         hit = gathered[:, :, 6] != 0
         zt = (gathered[:, :, 3] * hit).sum(0)
         out = torch.zeros(gathered.shape[1], 8, dtype=torch.float32)
-        out[:, 0] = big.float()
+        out[:, 0] = m.max(0).values.float()
+        out[:, 7] = big.float()
         out[:, 1] = s.float()
         out[:, 2] = t.float()
         out[:, 3] = zt
@@ -192,7 +195,8 @@ class CpuHeadOps:
     def finalize(self, stats, targets, n_grad, acc, acc_scale, w16, ld_w, col0, hidden_cols,
                  grad_rows, want_grad):
         n = stats.shape[0]
-        m, s, t, zt = (stats[:, i].double() for i in range(4))
+        s, t, zt = (stats[:, i].double() for i in range(1, 4))
+        m = stats[:, 7].double()             # lse = ref + log(s)
         idx = stats[:, 5].contiguous().view(torch.int32).to(torch.int64)
         labelled = targets >= 0
         ls = torch.log(s)

@@ -41,6 +41,9 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;     // double-buffered fp32 accumulator
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
 constexpr float kLog2e = 1.4426950408889634f;
+// Slack of the lazy reference: a row's probabilities and accumulator stay relative to REF while
+// its running max is at most REF + kRefSlack, so p = exp(z - REF) <= e^8 (fits fp16).
+constexpr float kRefSlack = 8.0f;
 
 constexpr uint32_t kIdescLogits = idesc_f16_f32(BM, BN, false, false);  // A, B K-major
 constexpr uint32_t kIdescAccum = idesc_f16_f32(BM, BN, false, true);    // B (W) MN-major
@@ -98,6 +101,7 @@ struct LogitsParams {
   int n_col_tiles;    // ceil(cols / BN)
   int n_row_tiles;    // ceil(n_tokens / BM)
   long long col_base; // global column id of slice column 0
+  int has_ref;        // 0 on the first slice: no reference yet
   const long long* targets;
   float4* partial;    // [n_tokens][n_col_tiles]: m_t, s_t, t_t, first argmax (int bits)
   __half* probs;      // [n_grad][ldp]
@@ -121,7 +125,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&ctl->tfull[a], 1);
-      mbar_init(&ctl->tempty[a], 128);
+      mbar_init(&ctl->tempty[a], 4);  // one arrive per epilogue warp
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
@@ -198,7 +202,8 @@ __global__ void __launch_bounds__(192, 1)
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
       const int rt = tile % p.n_row_tiles, ct = tile / p.n_row_tiles;
-      if (!mbar_wait(&ctl->tfull[acc], acc_phase, abort)) break;
+      // warp-uniform decision (each lane's wait is bounded, so every lane reaches the vote)
+      if (!__all_sync(0xffffffffu, mbar_wait(&ctl->tfull[acc], acc_phase, abort))) break;
       tc_fence_after();
       const int row = rt * BM + r_in_tile;
       const bool valid_row = row < p.n_tokens;
@@ -226,11 +231,17 @@ __global__ void __launch_bounds__(192, 1)
           if (col == tcol) zt = z;
         }
       }
-      // pass 2: sums relative to the tile max; probabilities of labelled rows
+      // pass 2: sums and probabilities relative to the row's reference when the tile max stays
+      // within its slack (the common case), else relative to the tile max; the combine kernel
+      // recomputes the same choice from (mx, REF)
+      const float ref = (p.has_ref && valid_row)
+                            ? p.stats[static_cast<long long>(row) * TALM_HEAD_STATS + TALM_STAT_REF]
+                            : 0.0f;
+      const float base = (p.has_ref && mx <= ref + kRefSlack) ? ref : mx;
       float s = 0.0f, t = 0.0f;
       const bool write_p = row < p.n_grad;
       __half* prow = p.probs + static_cast<long long>(row) * p.ldp + static_cast<long long>(ct) * BN;
-      const float mscaled = mx * kLog2e;
+      const float mscaled = base * kLog2e;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         tmem_ld_32x32b_x32(taddr + c * 32, r);
@@ -257,7 +268,8 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&ctl->tempty[acc]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->tempty[acc]);
       if (valid_row) {
         p.partial[static_cast<long long>(row) * p.n_col_tiles + ct] =
             make_float4(mx, s, t, __int_as_float(static_cast<int>(tile_col0 + arg)));
@@ -290,11 +302,21 @@ __global__ void __launch_bounds__(256) head_combine_kernel(const float4* __restr
                                                            int n_grad, int first,
                                                            float* __restrict__ stats,
                                                            float* __restrict__ tile_scale,
-                                                           float* __restrict__ alpha) {
+                                                           float* __restrict__ alpha,
+                                                           int* __restrict__ block_jump) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
   if (row >= n_tokens) return;
   const float4* pr = partial + static_cast<long long>(row) * n_col_tiles;
+  float* st = stats + static_cast<long long>(row) * TALM_HEAD_STATS;
+  // every lane reads the running statistics before lane 0 overwrites them
+  const float ref = first ? 0.0f : st[TALM_STAT_REF];
+  const float m_old = first ? -INFINITY : st[TALM_STAT_M];
+  const float s_old = first ? 0.0f : st[TALM_STAT_S];
+  const float t_old = first ? 0.0f : st[TALM_STAT_T];
+  const float best_old = first ? -INFINITY : st[TALM_STAT_BEST];
+  __syncwarp();
+  // the slice's max and first argmax
   float M = -INFINITY, bv = -INFINITY;
   int bi = 0x7fffffff;
   for (int j = lane; j < n_col_tiles; j += 32) {
@@ -309,53 +331,40 @@ __global__ void __launch_bounds__(256) head_combine_kernel(const float4* __restr
     const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
     better_arg(bv, bi, v2, i2);
   }
+  const float m_new = fmaxf(m_old, M);
+  // the reference moves (a "jump") on the first slice and when the max outgrows its slack
+  const bool jump = first || m_new > ref + kRefSlack;
+  const float ref_new = jump ? m_new : ref;
+  // tile sums were taken relative to base_j = (has ref and m_j <= ref + slack) ? ref : m_j
   float S = 0.0f, T = 0.0f;
+  float* sc = tile_scale + static_cast<long long>(row) * n_col_tiles;
   for (int j = lane; j < n_col_tiles; j += 32) {
     const float4 v = pr[j];
-    const float w = ex2((v.x - M) * kLog2e);
+    const float base = (!first && v.x <= ref + kRefSlack) ? ref : v.x;
+    const float w = ex2((base - ref_new) * kLog2e);
     S = fmaf(v.y, w, S);
     T = fmaf(v.z, w, T);
+    if (row < n_grad) sc[j] = w;  // the accumulator GEMM's factor for this tile (1 if stable)
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     S += __shfl_xor_sync(0xffffffffu, S, o);
     T += __shfl_xor_sync(0xffffffffu, T, o);
   }
-  float* st = stats + static_cast<long long>(row) * TALM_HEAD_STATS;
-  // every lane reads the running statistics before lane 0 overwrites them
-  const float m_old = first ? -INFINITY : st[TALM_STAT_M];
-  const float s_old = first ? 0.0f : st[TALM_STAT_S];
-  const float t_old = first ? 0.0f : st[TALM_STAT_T];
-  const float best_old = first ? -INFINITY : st[TALM_STAT_BEST];
-  __syncwarp();
-  float m_new, a = 0.0f;
-  if (first) {
-    m_new = M;
-    if (lane == 0) {
-      st[TALM_STAT_M] = M;
-      st[TALM_STAT_S] = S;
-      st[TALM_STAT_T] = T;
+  const float a = first ? 0.0f : ex2((ref - ref_new) * kLog2e);
+  if (lane == 0) {
+    st[TALM_STAT_REF] = ref_new;
+    st[TALM_STAT_M] = m_new;
+    st[TALM_STAT_S] = s_old * a + S;
+    st[TALM_STAT_T] = t_old * a + T;
+    if (first || bv > best_old) {  // earlier slices win ties: lower columns
       st[TALM_STAT_BEST] = bv;
       st[TALM_STAT_IDX] = __int_as_float(bi);
     }
-  } else {
-    m_new = fmaxf(m_old, M);
-    a = ex2((m_old - m_new) * kLog2e);
-    const float b = ex2((M - m_new) * kLog2e);
-    if (lane == 0) {
-      st[TALM_STAT_M] = m_new;
-      st[TALM_STAT_S] = s_old * a + S * b;
-      st[TALM_STAT_T] = t_old * a + T * b;
-      if (bv > best_old) {  // earlier slices win ties: lower columns
-        st[TALM_STAT_BEST] = bv;
-        st[TALM_STAT_IDX] = __int_as_float(bi);
-      }
+    if (row < n_grad) {
+      alpha[row] = a;
+      if (jump) atomicOr(block_jump + row / BM, 1);
     }
-  }
-  if (row < n_grad) {
-    if (lane == 0) alpha[row] = a;
-    float* sc = tile_scale + static_cast<long long>(row) * n_col_tiles;
-    for (int j = lane; j < n_col_tiles; j += 32) sc[j] = ex2((pr[j].x - m_new) * kLog2e);
   }
 }
 
@@ -373,6 +382,7 @@ struct AccumParams {
   int first;
   const float* tile_scale;  // [n_grad][n_col_tiles]
   const float* alpha;       // [n_grad]
+  const int* block_jump;    // [n_row_tiles]: some row of the block moved its reference
   float* acc;               // [n_grad][hidden]
 };
 
@@ -388,12 +398,12 @@ __global__ void __launch_bounds__(320, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&ctl->full[s], 1);
-      mbar_init(&ctl->ready[s], 128);
+      mbar_init(&ctl->ready[s], 4);  // one arrive per transform warp
       mbar_init(&ctl->empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&ctl->tfull[a], 1);
-      mbar_init(&ctl->tempty[a], 128);
+      mbar_init(&ctl->tempty[a], 4);  // one arrive per epilogue warp
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
@@ -418,7 +428,7 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t phase = 0;
       int issued = 0;
       for (int tile = blockIdx.x; tile < n_tiles && !*abort; tile += gridDim.x) {
-        const int rt = tile % p.n_row_tiles, ht = tile / p.n_row_tiles;
+        const int ht = tile % p.n_h_tiles, rt = tile / p.n_h_tiles;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort)) break;
           uint8_t* a = smem + stage * STAGE_BYTES;
@@ -440,13 +450,24 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
+      uint32_t ready_phase = 0;  // bit s: parity of the next phase of ready[s]
       for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
         if (!mbar_wait(&ctl->tempty[acc], acc_phase ^ 1, abort)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
+        // tiles whose rows all kept their reference need no rescaling: the MMA consumes the
+        // TMA'd stage directly; otherwise it waits for the transform warps
+        const bool transformed = __ldg(p.block_jump + tile / p.n_h_tiles) != 0;
         bool ok = true;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!mbar_wait(&ctl->ready[stage], phase, abort)) { ok = false; break; }
+          bool landed;
+          if (transformed) {
+            landed = mbar_wait(&ctl->ready[stage], (ready_phase >> stage) & 1u, abort);
+            ready_phase ^= 1u << stage;
+          } else {
+            landed = mbar_wait(&ctl->full[stage], phase, abort);
+          }
+          if (!landed) { ok = false; break; }
           tc_fence_after();
           const uint32_t a = smem_u32(smem + stage * STAGE_BYTES);
           const uint32_t b = a + A_BYTES;
@@ -455,7 +476,8 @@ __global__ void __launch_bounds__(320, 1)
             // A: K-major rows of 128 B, +32 B per 16 K. B: MN-major, 64-wide hidden groups of
             // BK rows x 128 B (LBO = 8 KiB), 16 K-rows = +2 KiB.
             umma_f16(d, smem_desc_sw128(a + k * 32, 16, 1024),
-                     smem_desc_sw128(b + k * 2048, 64 * BK * 2, 1024), kIdescAccum, (kb | k) != 0);
+                     smem_desc_sw128(b + k * 2048, 64 * BK * 2, 1024), kIdescAccum,
+                     (kb | k) != 0);
           }
           umma_commit(&ctl->empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -472,16 +494,30 @@ __global__ void __launch_bounds__(320, 1)
     int stage = 0;
     uint32_t phase = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-      const int rt = tile % p.n_row_tiles;
+      const int rt = tile / p.n_h_tiles;
+      if (__ldg(p.block_jump + rt) == 0) {  // the MMA consumes these stages untouched
+        const int adv = p.k_blocks % STAGES;
+        phase ^= static_cast<uint32_t>((p.k_blocks / STAGES) & 1);
+        if (stage + adv >= STAGES) phase ^= 1;
+        stage = (stage + adv) % STAGES;
+        continue;
+      }
       const int row = min(rt * BM + r_in_tile, p.n_grad - 1);
       const float* sc_row = p.tile_scale + static_cast<long long>(row) * p.n_col_tiles;
       bool ok = true;
       for (int kb = 0; kb < p.k_blocks; ++kb) {
-        if (!mbar_wait(&ctl->full[stage], phase, abort)) { ok = false; break; }
+        if (!__all_sync(0xffffffffu, mbar_wait(&ctl->full[stage], phase, abort))) {
+          ok = false;
+          break;
+        }
         const float sc = __ldg(sc_row + (kb * BK) / BN);
         uint4* line = reinterpret_cast<uint4*>(smem + stage * STAGE_BYTES + r_in_tile * 128);
+        // Visit the row's 16-byte chunks in logical order: logical chunk c sits at c ^ (row & 7)
+        // (128-byte swizzle), so the 32 lanes of a warp spread over all 8 chunk positions and
+        // each 512-byte warp access takes the minimum 4 shared-memory wavefronts.
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int c0 = 0; c0 < 8; ++c0) {
+          const int c = c0 ^ (r_in_tile & 7);
           uint4 v = line[c];
           uint32_t* w = reinterpret_cast<uint32_t*>(&v);
 #pragma unroll
@@ -493,7 +529,8 @@ __global__ void __launch_bounds__(320, 1)
           line[c] = v;
         }
         fence_proxy_async_smem();
-        mbar_arrive(&ctl->ready[stage]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->ready[stage]);
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
       if (!ok) break;
@@ -504,8 +541,9 @@ __global__ void __launch_bounds__(320, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-      const int rt = tile % p.n_row_tiles, ht = tile / p.n_row_tiles;
-      if (!mbar_wait(&ctl->tfull[acc], acc_phase, abort)) break;
+      const int ht = tile % p.n_h_tiles, rt = tile / p.n_h_tiles;
+      // warp-uniform decision (each lane's wait is bounded, so every lane reaches the vote)
+      if (!__all_sync(0xffffffffu, mbar_wait(&ctl->tfull[acc], acc_phase, abort))) break;
       tc_fence_after();
       const int row = rt * BM + r_in_tile;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
@@ -547,7 +585,8 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&ctl->tempty[acc]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->tempty[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
@@ -576,12 +615,12 @@ __global__ void __launch_bounds__(256) head_finalize_kernel(
   const long long tgt = targets[row];
   const bool labelled = tgt >= 0;
   const long long out = grad_rows ? grad_rows[row] : row;
-  const float m = st[TALM_STAT_M], s = st[TALM_STAT_S], t = st[TALM_STAT_T];
+  const float ref = st[TALM_STAT_REF], s = st[TALM_STAT_S], t = st[TALM_STAT_T];
   if (lane == 0) {
     const float ls = logf(s);
-    const float lse = m + ls;
+    const float lse = ref + ls;
     if (token_entropy) token_entropy[out] = lse - t / s;
-    if (token_loss) token_loss[out] = labelled ? ls + (m - st[TALM_STAT_ZT]) : 0.0f;
+    if (token_loss) token_loss[out] = labelled ? ls + (ref - st[TALM_STAT_ZT]) : 0.0f;
     if (correct)
       correct[out] = (labelled && static_cast<long long>(__float_as_int(st[TALM_STAT_IDX])) == tgt)
                          ? 1 : 0;
@@ -617,18 +656,19 @@ __global__ void __launch_bounds__(256) head_merge_shards_kernel(const float* __r
                                                                 float* __restrict__ acc_scale) {
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= n_tokens) return;
-  float M = -INFINITY, bv = -INFINITY, zt = 0.0f, hit = 0.0f;
+  float M = -INFINITY, R = -INFINITY, bv = -INFINITY, zt = 0.0f, hit = 0.0f;
   int bi = 0x7fffffff;
   for (int r = 0; r < n_shards; ++r) {
     const float* st = gathered + (static_cast<long long>(r) * n_tokens + row) * TALM_HEAD_STATS;
     M = fmaxf(M, st[TALM_STAT_M]);
+    R = fmaxf(R, st[TALM_STAT_REF]);
     better_arg(bv, bi, st[TALM_STAT_BEST], __float_as_int(st[TALM_STAT_IDX]));
     if (st[TALM_STAT_HIT] != 0.0f) { zt = st[TALM_STAT_ZT]; hit = 1.0f; }
   }
   float S = 0.0f, T = 0.0f, mine = 0.0f;
   for (int r = 0; r < n_shards; ++r) {
     const float* st = gathered + (static_cast<long long>(r) * n_tokens + row) * TALM_HEAD_STATS;
-    const float w = ex2((st[TALM_STAT_M] - M) * kLog2e);
+    const float w = ex2((st[TALM_STAT_REF] - R) * kLog2e);
     S = fmaf(st[TALM_STAT_S], w, S);
     T = fmaf(st[TALM_STAT_T], w, T);
     if (r == rank) mine = w;
@@ -641,7 +681,7 @@ __global__ void __launch_bounds__(256) head_merge_shards_kernel(const float* __r
   o[TALM_STAT_BEST] = bv;
   o[TALM_STAT_IDX] = __int_as_float(bi);
   o[TALM_STAT_HIT] = hit;
-  o[TALM_STAT_PAD] = 0.0f;
+  o[TALM_STAT_REF] = R;
   if (acc_scale != nullptr && row < n_grad) acc_scale[row] = mine / S;
 }
 
@@ -653,6 +693,7 @@ struct Workspace {
   float4* partial;
   float* tile_scale;
   float* alpha;
+  int* block_jump;  // [n_slices][ceil(n_grad / BM)]
   size_t bytes;
 };
 
@@ -679,6 +720,9 @@ Workspace layout(int64_t n_tokens, int64_t n_grad, int64_t vocab_cols, int64_t v
   off = align_up(off + static_cast<size_t>(n_grad) * tiles * 4, 256);
   w.alpha = reinterpret_cast<float*>(base + off);
   off = align_up(off + static_cast<size_t>(n_grad) * 4, 256);
+  w.block_jump = reinterpret_cast<int*>(base + off);
+  const int64_t n_slices = (vocab_cols + chunk - 1) / chunk;
+  off = align_up(off + static_cast<size_t>(n_slices) * ((n_grad + BM - 1) / BM + 1) * 4, 256);
   w.bytes = off + 256;  // slack for base alignment
   return w;
 }
@@ -755,6 +799,10 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
 
   if (cudaMemsetAsync(stats, 0, sizeof(float) * TALM_HEAD_STATS * n_tokens, stream) != cudaSuccess)
     return check_launch("stats memset");
+  const int64_t n_slices = (vocab_cols + chunk - 1) / chunk;
+  const int64_t flag_stride = (n_grad + BM - 1) / BM + 1;
+  if (cudaMemsetAsync(ws.block_jump, 0, sizeof(int) * n_slices * flag_stride, stream) != cudaSuccess)
+    return check_launch("flag memset");
 
   const int k_blocks = static_cast<int>((hidden_size + BK - 1) / BK);
   const int n_row_tiles = static_cast<int>((n_tokens + BM - 1) / BM);
@@ -770,6 +818,8 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
     lp.n_col_tiles = n_col_tiles;
     lp.n_row_tiles = n_row_tiles;
     lp.col_base = vocab_col0 + s0;
+    lp.has_ref = s0 != 0;
+    int* slice_jump = ws.block_jump + (s0 / chunk) * flag_stride;
     lp.targets = reinterpret_cast<const long long*>(targets);
     lp.partial = ws.partial;
     lp.probs = ws.probs;
@@ -787,7 +837,7 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
     LaunchTimer timer(TALM_KERNEL_HEAD_COMBINE, stream);
     head_combine_kernel<<<static_cast<int>((n_tokens + 7) / 8), 256, 0, stream>>>(
         ws.partial, n_col_tiles, static_cast<int>(n_tokens), static_cast<int>(n_grad), s0 == 0,
-        stats, ws.tile_scale, ws.alpha);
+        stats, ws.tile_scale, ws.alpha, slice_jump);
     }
     if ((st = check_launch("head combine kernel")) != TALM_OK) return st;
 
@@ -803,6 +853,7 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
       ap.first = s0 == 0;
       ap.tile_scale = ws.tile_scale;
       ap.alpha = ws.alpha;
+      ap.block_jump = slice_jump;
       ap.acc = acc;
       const int atiles = ap.n_row_tiles * ap.n_h_tiles;
       LaunchTimer timer(TALM_KERNEL_HEAD_ACCUM, stream);
