@@ -144,6 +144,21 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
                     int64_t vocab_chunk, float* stats, float* acc, void* workspace,
                     size_t ws_bytes, void* stream);
 
+/* talm_head_shard with no workspace argument, for callers that cannot allocate device memory
+ * where they call the head (a fixed memory plan that must not grow, an allocator owned by
+ * another runtime, a C caller with no allocator binding). No counterpart in the reference: its
+ * head allocates its temporaries through PyTorch. The scratch is a static 16 MiB device array
+ * inside this library, held on every GPU that loads it until the process exits; calls needing
+ * more scratch than that (talm_head_workspace_size) return TALM_ERANGE before enqueuing
+ * anything. The first call on a device looks up the array's device address (make it before any
+ * stream capture). All calls on a device share the scratch: calls whose kernels overlap on the
+ * GPU race and must be ordered by the caller. Everything else is as talm_head_shard. */
+int talm_head_shard_noalloc(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* weight,
+                            int64_t ld_weight, const int64_t* targets, int64_t n_tokens,
+                            int64_t n_grad, int64_t hidden_size, int64_t vocab_cols,
+                            int64_t vocab_col0, int64_t vocab_chunk, float* stats, float* acc,
+                            void* stream);
+
 /* Per-row outputs and the hidden gradient from complete statistics (one shard covering the
  * whole vocabulary, or the combination of all shards).
  * Replaces the last-slice branch of `fused_head_vocab_kernel` (fused_head.py:160-169) and its

@@ -3,3 +3,4 @@
 #include "abi.cu"
 #include "nf4.cu"
 #include "head.cu"
+#include "head_noalloc.cu"
