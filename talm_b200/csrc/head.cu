@@ -26,6 +26,8 @@
 // writing rows in the caller's original order.
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace talm {
@@ -62,9 +64,53 @@ struct SharedCtl {
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t drain;          // MMA issuer: every UMMA issued has completed
+  uint64_t ring_full[4];   // tile-id ring (dynamic scheduler): id published
+  uint64_t ring_empty[4];  // every consumer role has read the id
+  int ring_id[4];
   uint32_t tmem_base;
   int abort;
 };
+
+// Dynamic tile scheduler. The TMA thread claims tiles from a global counter (one per launch,
+// zeroed by the host) and publishes each id through a 4-slot ring in shared memory; the MMA
+// thread and the epilogue / transform warps read the same sequence. CTAs that start late (the
+// other kernel of the pipeline still holds their SM) simply claim fewer tiles.
+__device__ __forceinline__ int ring_publish(SharedCtl* ctl, int i, int* counter, int n_tiles,
+                                            volatile int* abort) {
+  const int slot = i & 3;
+  if (!mbar_wait(&ctl->ring_empty[slot], ((i >> 2) & 1) ^ 1, abort)) return -1;
+  int tile = atomicAdd(counter, 1);
+  if (tile >= n_tiles) tile = -1;
+  ctl->ring_id[slot] = tile;
+  mbar_arrive(&ctl->ring_full[slot]);
+  return tile;
+}
+
+// One thread's read of ring entry i (then the caller releases the slot with ring_release).
+__device__ __forceinline__ int ring_take(SharedCtl* ctl, int i, volatile int* abort) {
+  const int slot = i & 3;
+  if (!mbar_wait(&ctl->ring_full[slot], (i >> 2) & 1, abort)) return -1;
+  return *reinterpret_cast<volatile int*>(&ctl->ring_id[slot]);
+}
+
+// A warp's read of ring entry i: every lane gets the id (or -1 when done / aborting), lane 0
+// releases the slot.
+__device__ __forceinline__ int ring_take_warp(SharedCtl* ctl, int i, volatile int* abort,
+                                              int lane) {
+  const int slot = i & 3;
+  if (!__all_sync(0xffffffffu, mbar_wait(&ctl->ring_full[slot], (i >> 2) & 1, abort))) return -1;
+  const int tile = *reinterpret_cast<volatile int*>(&ctl->ring_id[slot]);
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&ctl->ring_empty[slot]);
+  return tile;
+}
+
+__device__ __forceinline__ void init_ring(SharedCtl* ctl, int consumers) {
+  for (int r = 0; r < 4; ++r) {
+    mbar_init(&ctl->ring_full[r], 1);
+    mbar_init(&ctl->ring_empty[r], consumers);
+  }
+}
 
 __device__ __forceinline__ uint8_t* aligned_smem(uint8_t* raw) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
@@ -102,6 +148,7 @@ struct LogitsParams {
   int n_row_tiles;    // ceil(n_tokens / BM)
   long long col_base; // global column id of slice column 0
   int has_ref;        // 0 on the first slice: no reference yet
+  int* tile_counter;  // dynamic scheduler counter of this launch (zeroed by the host)
   const long long* targets;
   float4* partial;    // [n_tokens][n_col_tiles]: m_t, s_t, t_t, first argmax (int bits)
   __half* probs;      // [n_grad][ldp]
@@ -128,6 +175,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&ctl->tempty[a], 4);  // one arrive per epilogue warp
     }
     mbar_init(&ctl->drain, 1);
+    init_ring(ctl, 1 + 4);  // MMA thread + 4 epilogue warps
     ctl->abort = 0;
     fence_mbar_init();
     prefetch_tmap(&tm_hidden);
@@ -149,7 +197,9 @@ __global__ void __launch_bounds__(192, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
-      for (int tile = blockIdx.x; tile < n_tiles && !*abort; tile += gridDim.x) {
+      for (int i = 0;; ++i) {
+        const int tile = ring_publish(ctl, i, p.tile_counter, n_tiles, abort);
+        if (tile < 0) break;
         const int rt = tile % p.n_row_tiles, ct = tile / p.n_row_tiles;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort)) break;
@@ -170,7 +220,10 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+      for (int i = 0;; ++i) {
+        const int tile = ring_take(ctl, i, abort);
+        if (tile < 0) break;
+        mbar_arrive(&ctl->ring_empty[i & 3]);
         if (!mbar_wait(&ctl->tempty[acc], acc_phase ^ 1, abort)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
@@ -200,7 +253,9 @@ __global__ void __launch_bounds__(192, 1)
     const int r_in_tile = q * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    for (int i = 0;; ++i) {
+      const int tile = ring_take_warp(ctl, i, abort, lane);
+      if (tile < 0) break;
       const int rt = tile % p.n_row_tiles, ct = tile / p.n_row_tiles;
       // warp-uniform decision (each lane's wait is bounded, so every lane reaches the vote)
       if (!__all_sync(0xffffffffu, mbar_wait(&ctl->tfull[acc], acc_phase, abort))) break;
@@ -383,6 +438,7 @@ struct AccumParams {
   const float* tile_scale;  // [n_grad][n_col_tiles]
   const float* alpha;       // [n_grad]
   const int* block_jump;    // [n_row_tiles]: some row of the block moved its reference
+  int* tile_counter;        // dynamic scheduler counter of this launch (zeroed by the host)
   float* acc;               // [n_grad][hidden]
 };
 
@@ -406,6 +462,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&ctl->tempty[a], 4);  // one arrive per epilogue warp
     }
     mbar_init(&ctl->drain, 1);
+    init_ring(ctl, 1 + 4 + 4);  // MMA thread + 4 epilogue warps + 4 transform warps
     ctl->abort = 0;
     fence_mbar_init();
     prefetch_tmap(&tm_probs);
@@ -427,7 +484,9 @@ __global__ void __launch_bounds__(320, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
-      for (int tile = blockIdx.x; tile < n_tiles && !*abort; tile += gridDim.x) {
+      for (int i = 0;; ++i) {
+        const int tile = ring_publish(ctl, i, p.tile_counter, n_tiles, abort);
+        if (tile < 0) break;
         const int ht = tile % p.n_h_tiles, rt = tile / p.n_h_tiles;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort)) break;
@@ -451,7 +510,10 @@ __global__ void __launch_bounds__(320, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       uint32_t ready_phase = 0;  // bit s: parity of the next phase of ready[s]
-      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+      for (int i = 0;; ++i) {
+        const int tile = ring_take(ctl, i, abort);
+        if (tile < 0) break;
+        mbar_arrive(&ctl->ring_empty[i & 3]);
         if (!mbar_wait(&ctl->tempty[acc], acc_phase ^ 1, abort)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
@@ -493,7 +555,9 @@ __global__ void __launch_bounds__(320, 1)
     const int r_in_tile = (warp - 6) * 32 + lane;
     int stage = 0;
     uint32_t phase = 0;
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    for (int i = 0;; ++i) {
+      const int tile = ring_take_warp(ctl, i, abort, lane);
+      if (tile < 0) break;
       const int rt = tile / p.n_h_tiles;
       if (__ldg(p.block_jump + rt) == 0) {  // the MMA consumes these stages untouched
         const int adv = p.k_blocks % STAGES;
@@ -540,7 +604,9 @@ __global__ void __launch_bounds__(320, 1)
     const int r_in_tile = q * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    for (int i = 0;; ++i) {
+      const int tile = ring_take_warp(ctl, i, abort, lane);
+      if (tile < 0) break;
       const int ht = tile % p.n_h_tiles, rt = tile / p.n_h_tiles;
       // warp-uniform decision (each lane's wait is bounded, so every lane reaches the vote)
       if (!__all_sync(0xffffffffu, mbar_wait(&ctl->tfull[acc], acc_phase, abort))) break;
@@ -688,12 +754,15 @@ __global__ void __launch_bounds__(256) head_merge_shards_kernel(const float* __r
 // ------------------------------------------------------------------------------------------
 // host side
 // ------------------------------------------------------------------------------------------
+// Slice buffers come in pairs: the accumulator GEMM of slice k (side stream) reads pair k % 2
+// while the logits GEMM and the combine of slice k + 1 (caller's stream) write the other one.
 struct Workspace {
-  __half* probs;
-  float4* partial;
-  float* tile_scale;
-  float* alpha;
-  int* block_jump;  // [n_slices][ceil(n_grad / BM)]
+  __half* probs[2];      // [n_grad][chunk] each
+  float4* partial;       // [n_tokens][chunk / BN]
+  float* tile_scale[2];  // [n_grad][chunk / BN] each
+  float* alpha[2];       // [n_grad] each
+  int* block_jump;       // [n_slices][flag_stride]
+  int* counters;         // [n_slices][2]: dynamic scheduler counters (logits, accum)
   size_t bytes;
 };
 
@@ -710,21 +779,63 @@ Workspace layout(int64_t n_tokens, int64_t n_grad, int64_t vocab_cols, int64_t v
                  uint8_t* base) {
   const int64_t chunk = chunk_cols(vocab_cols, vocab_chunk);
   const int64_t tiles = chunk / BN;
+  const int64_t n_slices = (vocab_cols + chunk - 1) / chunk;
+  const int n_buf = n_slices > 1 ? 2 : 1;
   Workspace w;
   size_t off = 0;
-  w.probs = reinterpret_cast<__half*>(base + off);
-  off = align_up(off + static_cast<size_t>(n_grad) * chunk * 2, 256);
+  for (int b = 0; b < 2; ++b) {
+    w.probs[b] = reinterpret_cast<__half*>(base + off);
+    if (b < n_buf) off = align_up(off + static_cast<size_t>(n_grad) * chunk * 2, 256);
+  }
   w.partial = reinterpret_cast<float4*>(base + off);
   off = align_up(off + static_cast<size_t>(n_tokens) * tiles * 16, 256);
-  w.tile_scale = reinterpret_cast<float*>(base + off);
-  off = align_up(off + static_cast<size_t>(n_grad) * tiles * 4, 256);
-  w.alpha = reinterpret_cast<float*>(base + off);
-  off = align_up(off + static_cast<size_t>(n_grad) * 4, 256);
+  for (int b = 0; b < 2; ++b) {
+    w.tile_scale[b] = reinterpret_cast<float*>(base + off);
+    if (b < n_buf) off = align_up(off + static_cast<size_t>(n_grad) * tiles * 4, 256);
+  }
+  for (int b = 0; b < 2; ++b) {
+    w.alpha[b] = reinterpret_cast<float*>(base + off);
+    if (b < n_buf) off = align_up(off + static_cast<size_t>(n_grad) * 4, 256);
+  }
   w.block_jump = reinterpret_cast<int*>(base + off);
-  const int64_t n_slices = (vocab_cols + chunk - 1) / chunk;
   off = align_up(off + static_cast<size_t>(n_slices) * ((n_grad + BM - 1) / BM + 1) * 4, 256);
+  w.counters = reinterpret_cast<int*>(base + off);
+  off = align_up(off + static_cast<size_t>(n_slices) * 2 * 4, 256);
   w.bytes = off + 256;  // slack for base alignment
   return w;
+}
+
+// The accumulator GEMM runs on a library-owned stream per device, forked from and joined back
+// into the caller's stream with events, so that it overlaps the next slice's logits GEMM. The
+// stream and its events are created once per device; calls from several host threads serialise
+// their enqueueing on a mutex (the GPU work of the calls then orders on the side stream).
+struct SidePipe {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t combined[2] = {nullptr, nullptr};  // slice k's statistics ready (caller's stream)
+  cudaEvent_t drained[2] = {nullptr, nullptr};   // slice k's accumulator GEMM done (side stream)
+  bool ready = false;
+};
+constexpr int kMaxPipeDevices = 64;
+SidePipe g_pipes[kMaxPipeDevices];
+std::mutex g_pipe_mutex;
+
+int side_pipe(SidePipe** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxPipeDevices)
+    return set_error(TALM_ENODEV, "no usable current device");
+  SidePipe& p = g_pipes[dev];
+  if (!p.ready) {
+    cudaError_t e = cudaStreamCreateWithFlags(&p.stream, cudaStreamNonBlocking);
+    for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
+      e = cudaEventCreateWithFlags(&p.combined[i], cudaEventDisableTiming);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p.drained[i], cudaEventDisableTiming);
+    }
+    if (e != cudaSuccess)
+      return set_error(TALM_ECUDA, "side stream set-up: %s", cudaGetErrorString(e));
+    p.ready = true;
+  }
+  *out = &p;
+  return TALM_OK;
 }
 
 bool g_attrs_set = false;
@@ -787,28 +898,44 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
   const int64_t chunk = chunk_cols(vocab_cols, vocab_chunk);
   const int sms = current_sm_count();
 
-  CUtensorMap tm_hidden, tm_weight, tm_probs, tm_weight_mn;
+  CUtensorMap tm_hidden, tm_weight, tm_weight_mn;
   st = talm_make_tmap_2d_f16(&tm_hidden, hidden, hidden_size, n_tokens, ld_hidden, BK, BM);
   if (st == TALM_OK)
     st = talm_make_tmap_2d_f16(&tm_weight, weight, hidden_size, vocab_cols, ld_weight, BK, BN);
   if (st == TALM_OK && n_grad > 0)
-    st = talm_make_tmap_2d_f16(&tm_probs, ws.probs, chunk, n_grad, chunk, BK, BM);
-  if (st == TALM_OK && n_grad > 0)
     st = talm_make_tmap_2d_f16(&tm_weight_mn, weight, hidden_size, vocab_cols, ld_weight, 64, BK);
   if (st != TALM_OK) return st;
 
-  if (cudaMemsetAsync(stats, 0, sizeof(float) * TALM_HEAD_STATS * n_tokens, stream) != cudaSuccess)
-    return check_launch("stats memset");
   const int64_t n_slices = (vocab_cols + chunk - 1) / chunk;
   const int64_t flag_stride = (n_grad + BM - 1) / BM + 1;
-  if (cudaMemsetAsync(ws.block_jump, 0, sizeof(int) * n_slices * flag_stride, stream) != cudaSuccess)
+  std::lock_guard<std::mutex> lock(g_pipe_mutex);
+  // The accumulator GEMM goes to the side stream (overlapping the next slice's logits GEMM)
+  // only when it has fewer tiles than the GPU has SMs; a GEMM that fills the GPU on its own
+  // gains nothing from sharing it and runs in order on the caller's stream.
+  const int64_t grad_tiles = ((n_grad + BM - 1) / BM) * ((hidden_size + BN - 1) / BN);
+  SidePipe* pipe = nullptr;
+  if (n_grad > 0 && n_slices > 1 && grad_tiles < sms && (st = side_pipe(&pipe)) != TALM_OK)
+    return st;
+
+  if (cudaMemsetAsync(stats, 0, sizeof(float) * TALM_HEAD_STATS * n_tokens, stream) != cudaSuccess)
+    return check_launch("stats memset");
+  // flags and scheduler counters are contiguous in the workspace: one memset for both
+  const size_t zero_bytes = reinterpret_cast<uint8_t*>(ws.counters + n_slices * 2) -
+                            reinterpret_cast<uint8_t*>(ws.block_jump);
+  if (cudaMemsetAsync(ws.block_jump, 0, zero_bytes, stream) != cudaSuccess)
     return check_launch("flag memset");
 
   const int k_blocks = static_cast<int>((hidden_size + BK - 1) / BK);
   const int n_row_tiles = static_cast<int>((n_tokens + BM - 1) / BM);
-  for (int64_t s0 = 0; s0 < vocab_cols; s0 += chunk) {
+  for (int64_t k = 0; k < n_slices; ++k) {
+    const int64_t s0 = k * chunk;
+    const int buf = static_cast<int>(k & 1);
     const int cols = static_cast<int>(vocab_cols - s0 < chunk ? vocab_cols - s0 : chunk);
     const int n_col_tiles = (cols + BN - 1) / BN;
+    int* slice_jump = ws.block_jump + k * flag_stride;
+    // the pair of buffers this slice writes is free once slice k - 2's accumulator GEMM is done
+    if (pipe && k >= 2 && cudaStreamWaitEvent(stream, pipe->drained[buf], 0) != cudaSuccess)
+      return check_launch("wait for slice buffers");
     LogitsParams lp;
     lp.n_tokens = static_cast<int>(n_tokens);
     lp.n_grad = static_cast<int>(n_grad);
@@ -818,30 +945,37 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
     lp.n_col_tiles = n_col_tiles;
     lp.n_row_tiles = n_row_tiles;
     lp.col_base = vocab_col0 + s0;
-    lp.has_ref = s0 != 0;
-    int* slice_jump = ws.block_jump + (s0 / chunk) * flag_stride;
+    lp.has_ref = k != 0;
+    lp.tile_counter = ws.counters + 2 * k;
     lp.targets = reinterpret_cast<const long long*>(targets);
     lp.partial = ws.partial;
-    lp.probs = ws.probs;
+    lp.probs = ws.probs[buf];
     lp.ldp = chunk;
     lp.stats = stats;
     const int tiles = n_row_tiles * n_col_tiles;
     {
-    LaunchTimer timer(TALM_KERNEL_HEAD_LOGITS, stream);
-    head_logits_kernel<<<tiles < sms ? tiles : sms, 192, SMEM_BYTES, stream>>>(tm_hidden,
-                                                                             tm_weight, lp);
+      LaunchTimer timer(TALM_KERNEL_HEAD_LOGITS, stream);
+      head_logits_kernel<<<tiles < sms ? tiles : sms, 192, SMEM_BYTES, stream>>>(
+          tm_hidden, tm_weight, lp);
     }
     if ((st = check_launch("head logits kernel")) != TALM_OK) return st;
-
     {
-    LaunchTimer timer(TALM_KERNEL_HEAD_COMBINE, stream);
-    head_combine_kernel<<<static_cast<int>((n_tokens + 7) / 8), 256, 0, stream>>>(
-        ws.partial, n_col_tiles, static_cast<int>(n_tokens), static_cast<int>(n_grad), s0 == 0,
-        stats, ws.tile_scale, ws.alpha, slice_jump);
+      LaunchTimer timer(TALM_KERNEL_HEAD_COMBINE, stream);
+      head_combine_kernel<<<static_cast<int>((n_tokens + 7) / 8), 256, 0, stream>>>(
+          ws.partial, n_col_tiles, static_cast<int>(n_tokens), static_cast<int>(n_grad), k == 0,
+          stats, ws.tile_scale[buf], ws.alpha[buf], slice_jump);
     }
     if ((st = check_launch("head combine kernel")) != TALM_OK) return st;
 
     if (n_grad > 0) {
+      cudaStream_t acc_stream = pipe ? pipe->stream : stream;
+      if (pipe && (cudaEventRecord(pipe->combined[buf], stream) != cudaSuccess ||
+                   cudaStreamWaitEvent(pipe->stream, pipe->combined[buf], 0) != cudaSuccess))
+        return check_launch("fork to the side stream");
+      CUtensorMap tm_probs;
+      if ((st = talm_make_tmap_2d_f16(&tm_probs, ws.probs[buf], chunk, n_grad, chunk, BK, BM)) !=
+          TALM_OK)
+        return st;
       AccumParams ap;
       ap.n_grad = static_cast<int>(n_grad);
       ap.hidden = static_cast<int>(hidden_size);
@@ -850,18 +984,26 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
       ap.n_col_tiles = n_col_tiles;
       ap.n_row_tiles = static_cast<int>((n_grad + BM - 1) / BM);
       ap.n_h_tiles = static_cast<int>((hidden_size + BN - 1) / BN);
-      ap.first = s0 == 0;
-      ap.tile_scale = ws.tile_scale;
-      ap.alpha = ws.alpha;
+      ap.first = k == 0;
+      ap.tile_scale = ws.tile_scale[buf];
+      ap.alpha = ws.alpha[buf];
       ap.block_jump = slice_jump;
+      ap.tile_counter = ws.counters + 2 * k + 1;
       ap.acc = acc;
       const int atiles = ap.n_row_tiles * ap.n_h_tiles;
-      LaunchTimer timer(TALM_KERNEL_HEAD_ACCUM, stream);
-      head_accum_kernel<<<atiles < sms ? atiles : sms, 320, SMEM_BYTES, stream>>>(
-          tm_probs, tm_weight_mn, ap);
+      {
+        LaunchTimer timer(TALM_KERNEL_HEAD_ACCUM, acc_stream);
+        head_accum_kernel<<<atiles < sms ? atiles : sms, 320, SMEM_BYTES, acc_stream>>>(
+            tm_probs, tm_weight_mn, ap);
+      }
       if ((st = check_launch("head accumulator kernel")) != TALM_OK) return st;
+      if (pipe && cudaEventRecord(pipe->drained[buf], pipe->stream) != cudaSuccess)
+        return check_launch("side stream event");
     }
   }
+  // join: the caller's stream continues after the last accumulator GEMM
+  if (pipe && cudaStreamWaitEvent(stream, pipe->drained[(n_slices - 1) & 1], 0) != cudaSuccess)
+    return check_launch("join the side stream");
   return TALM_OK;
 }
 

@@ -70,38 +70,48 @@ __global__ void __launch_bounds__(256) nf4_chunks_kernel(const uint8_t* __restri
   const int64_t n_warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   const uint32_t* words = reinterpret_cast<const uint32_t*>(packed);
 
-  for (int64_t c = warp; c < n_chunks; c += n_warps) {
-    uint32_t w[4];
+  // Two chunks per iteration: all eight 128-byte loads of the pair are issued before any of
+  // them is consumed, so each warp keeps 1 KiB of reads in flight.
+  for (int64_t c = warp; c < n_chunks; c += 2 * n_warps) {
+    const int64_t cc[2] = {c, c + n_warps};
+    const bool second = cc[1] < n_chunks;
+    uint32_t w[2][4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) w[k] = ld_stream_u32(words + c * 128 + k * 32 + lane);
-
-    float sc[4];
-    const int64_t e0 = c * 1024;  // first element of the chunk
-    if constexpr (kWarpScale) {
-      const int64_t b0 = block_shift >= 0 ? (e0 >> block_shift) : e0 / blocksize;
-      const float mine = (lane <= 16 && b0 + lane < n_blocks) ? scale(b0 + lane) : 0.0f;
+    for (int k = 0; k < 4; ++k) w[0][k] = ld_stream_u32(words + cc[0] * 128 + k * 32 + lane);
+    if (second) {
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int64_t e = e0 + static_cast<int64_t>(k * 32 + lane) * 8;
-        const int64_t b = block_shift >= 0 ? (e >> block_shift) : e / blocksize;
-        sc[k] = __shfl_sync(0xffffffffu, mine, static_cast<int>(b - b0));
-      }
-    } else {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int64_t e = e0 + static_cast<int64_t>(k * 32 + lane) * 8;
-        sc[k] = scale(block_shift >= 0 ? (e >> block_shift) : e / blocksize);
-      }
+      for (int k = 0; k < 4; ++k) w[1][k] = ld_stream_u32(words + cc[1] * 128 + k * 32 + lane);
     }
-
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const uint32_t v = w[k];
-      const uint32_t p0 = nf4_pair(lut, v & 0xffu, sc[k]);
-      const uint32_t p1 = nf4_pair(lut, (v >> 8) & 0xffu, sc[k]);
-      const uint32_t p2 = nf4_pair(lut, (v >> 16) & 0xffu, sc[k]);
-      const uint32_t p3 = nf4_pair(lut, v >> 24, sc[k]);
-      st_v4(out_pairs + (c * 128 + k * 32 + lane) * 4, p0, p1, p2, p3);
+    for (int h = 0; h < 2; ++h) {
+      if (h == 1 && !second) break;
+      float sc[4];
+      const int64_t e0 = cc[h] * 1024;  // first element of the chunk
+      if constexpr (kWarpScale) {
+        const int64_t b0 = block_shift >= 0 ? (e0 >> block_shift) : e0 / blocksize;
+        const float mine = (lane <= 16 && b0 + lane < n_blocks) ? scale(b0 + lane) : 0.0f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int64_t e = e0 + static_cast<int64_t>(k * 32 + lane) * 8;
+          const int64_t b = block_shift >= 0 ? (e >> block_shift) : e / blocksize;
+          sc[k] = __shfl_sync(0xffffffffu, mine, static_cast<int>(b - b0));
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int64_t e = e0 + static_cast<int64_t>(k * 32 + lane) * 8;
+          sc[k] = scale(block_shift >= 0 ? (e >> block_shift) : e / blocksize);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t v = w[h][k];
+        const uint32_t p0 = nf4_pair(lut, v & 0xffu, sc[k]);
+        const uint32_t p1 = nf4_pair(lut, (v >> 8) & 0xffu, sc[k]);
+        const uint32_t p2 = nf4_pair(lut, (v >> 16) & 0xffu, sc[k]);
+        const uint32_t p3 = nf4_pair(lut, v >> 24, sc[k]);
+        st_v4(out_pairs + (cc[h] * 128 + k * 32 + lane) * 4, p0, p1, p2, p3);
+      }
     }
   }
 }
@@ -150,17 +160,20 @@ int run_nf4(const uint8_t* packed, uint16_t* out, int64_t n_elems, int64_t block
     const int64_t n_chunks = n_bytes / 512;
     if (n_chunks > 0) {
       const int shift = log2_exact(blocksize);
-      const int64_t want = (n_chunks + 7) / 8;  // 8 warps per block
-      const int grid = static_cast<int>(want < int64_t{sms} * 8 ? want : int64_t{sms} * 8);
       uint32_t* pairs = reinterpret_cast<uint32_t*>(out);
+      // one resident wave: SMs x the blocks per SM the kernel's registers allow
+      auto kernel = blocksize >= 64 ? nf4_chunks_kernel<Scale, true>
+                                    : nf4_chunks_kernel<Scale, false>;
+      int per_sm = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, 0) != cudaSuccess ||
+          per_sm < 1)
+        per_sm = 4;
+      const int64_t want = (n_chunks + 15) / 16;  // 8 warps per block, 2 chunks per warp
+      const int64_t cap = int64_t{sms} * per_sm;
+      const int grid = static_cast<int>(want < cap ? want : cap);
       LaunchTimer timer(TALM_KERNEL_NF4, stream);
-      if (blocksize >= 64) {
-        nf4_chunks_kernel<Scale, true><<<grid, 256, 0, stream>>>(
-            packed, pairs, n_chunks, n_blocks, shift, blocksize, scale, levels);
-      } else {
-        nf4_chunks_kernel<Scale, false><<<grid, 256, 0, stream>>>(
-            packed, pairs, n_chunks, n_blocks, shift, blocksize, scale, levels);
-      }
+      kernel<<<grid, 256, 0, stream>>>(packed, pairs, n_chunks, n_blocks, shift, blocksize, scale,
+                                      levels);
       int st = check_launch("nf4 chunk kernel");
       if (st != TALM_OK) return st;
       done = n_chunks * 512;

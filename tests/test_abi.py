@@ -80,5 +80,8 @@ def test_argument_errors_are_reported_before_any_launch(lib):
 def test_workspace_size_is_host_only(lib):
     size = ctypes.c_size_t(0)
     assert lib.talm_head_workspace_size(2048, 1126, 1536, 151936, 8192, ctypes.byref(size)) == 0
-    # P slice (n_grad x chunk fp16) dominates: 1126 * 8192 * 2 bytes
-    assert 1126 * 8192 * 2 < size.value < 1126 * 8192 * 2 + 4 * 2**20
+    # the pair of probability slices (2 x n_grad x chunk fp16) dominates
+    assert 2 * 1126 * 8192 * 2 < size.value < 2 * 1126 * 8192 * 2 + 4 * 2**20
+    # a single slice needs a single buffer
+    assert lib.talm_head_workspace_size(64, 64, 64, 1000, 8192, ctypes.byref(size)) == 0
+    assert 64 * 1024 * 2 < size.value < 2 * 64 * 1024 * 2
