@@ -95,20 +95,37 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
+static int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, uint64_t elem_bytes,
+                        const void* base, uint64_t inner, uint64_t outer,
+                        uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer);
+
 int talm_make_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                           uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer) {
+  return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, inner, outer,
+                      row_stride_elems, box_inner, box_outer);
+}
+
+int talm_make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                          uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer) {
+  return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, inner, outer,
+                      row_stride_elems, box_inner, box_outer);
+}
+
+static int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, uint64_t elem_bytes,
+                        const void* base, uint64_t inner, uint64_t outer,
+                        uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return talm::set_error(TALM_ENODEV, "cuTensorMapEncodeTiled unavailable");
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
     return talm::set_error(TALM_EINVAL, "TMA base address %p is not 16-byte aligned", base);
-  if ((row_stride_elems * 2) % 16 != 0)
-    return talm::set_error(TALM_EINVAL, "TMA row stride of %llu fp16 is not a multiple of 16 B",
+  if ((row_stride_elems * elem_bytes) % 16 != 0)
+    return talm::set_error(TALM_EINVAL, "TMA row stride of %llu elements is not a multiple of 16 B",
                            (unsigned long long)row_stride_elems);
   cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {row_stride_elems * 2};
+  cuuint64_t strides[1] = {row_stride_elems * elem_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
+  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)

@@ -33,22 +33,39 @@
 namespace talm {
 namespace head {
 
-constexpr int BM = 128;  // token rows per tile = TMEM lanes
-constexpr int BN = 256;  // columns per tile (vocab in the logits GEMM, hidden in the acc GEMM)
+constexpr int BM = 128;  // token rows per CTA = TMEM lanes; a CTA pair covers 2 * BM rows
+constexpr int PAIR_ROWS = 2 * BM;
+constexpr int BN = 256;  // columns of a pair tile (vocab in the logits GEMM, hidden in the acc GEMM)
 constexpr int BK = 64;   // K per pipeline stage: one 128-byte swizzle row of fp16
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2;  // 16 KiB
-constexpr int B_BYTES = BN * BK * 2;  // 32 KiB
+constexpr int STAGES = 5;
+constexpr int A_BYTES = BM * BK * 2;        // 16 KiB: this CTA's 128 rows of A
+constexpr int B_BYTES = (BN / 2) * BK * 2;  // 16 KiB: this CTA's half of B's columns
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int TMEM_COLS = 2 * BN;     // double-buffered fp32 accumulator
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+constexpr int TMEM_COLS = 2 * BN;           // double-buffered fp32 accumulator (128 x 256 per CTA)
+// Epilogue staging: two 16 KiB buffers (128 rows x 128 bytes, 128-byte swizzle) through which
+// the epilogue's outputs leave by TMA store / reduce-add instead of per-lane global stores.
+constexpr int STAGING_BYTES = 2 * 16384;
+constexpr int SMEM_BYTES =
+    STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align slack*/ + 512 /*barriers*/;
+// Two epilogue groups of 4 warps (one warp per TMEM lane quarter in each group); group g owns
+// columns [g * 128, g * 128 + 128) of the tile, so two warps per SM sub-partition interleave
+// and hide each other's latencies. Each group has its own named barrier (ids 1, 2), staging
+// buffer and TMA-issuing thread; per row and tile it leaves one statistics record ("part").
+constexpr int EPI_GROUPS = 2;
+constexpr int EPI_COLS = BN / EPI_GROUPS;      // 128 columns per group
+constexpr int EPI_WARPS = 4 * EPI_GROUPS;      // 8
+constexpr int EPI_THREADS = 128;               // threads per group
+constexpr int PARTS = EPI_GROUPS;              // statistics records per (row, tile)
+constexpr int LOGITS_THREADS = 32 * (2 + EPI_WARPS);       // producer, MMA, epilogue
+constexpr int ACCUM_THREADS = 32 * (2 + EPI_WARPS + 4);    // + 4 transform warps
 constexpr float kLog2e = 1.4426950408889634f;
 // Slack of the lazy reference: a row's probabilities and accumulator stay relative to REF while
 // its running max is at most REF + kRefSlack, so p = exp(z - REF) <= e^8 (fits fp16).
 constexpr float kRefSlack = 8.0f;
 
-constexpr uint32_t kIdescLogits = idesc_f16_f32(BM, BN, false, false);  // A, B K-major
-constexpr uint32_t kIdescAccum = idesc_f16_f32(BM, BN, false, true);    // B (W) MN-major
+// M = 256 across the CTA pair, N = 256 (128 columns of B in each CTA's shared memory)
+constexpr uint32_t kIdescLogits = idesc_f16_f32(PAIR_ROWS, BN, false, false);  // A, B K-major
+constexpr uint32_t kIdescAccum = idesc_f16_f32(PAIR_ROWS, BN, false, true);    // B (W) MN-major
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -57,69 +74,70 @@ __device__ __forceinline__ float ex2(float x) {
 }
 __device__ __forceinline__ float round_f16(float v) { return __half2float(__float2half_rn(v)); }
 
+// Barriers of a CTA of a pair. The pair leader (cluster rank 0) issues every MMA; `full`,
+// `ready` and `tempty` are waited on in the leader only and receive arrivals / transaction
+// bytes from both CTAs; `empty`, `afull` and `tfull` live in each CTA.
 struct SharedCtl {
-  uint64_t full[STAGES];
-  uint64_t ready[STAGES];  // accum kernel: stage transformed and ready for the MMA
-  uint64_t empty[STAGES];
-  uint64_t tfull[2];
-  uint64_t tempty[2];
+  uint64_t full[STAGES];   // leader: both CTAs' operands of the stage landed (TMA bytes)
+  uint64_t afull[STAGES];  // accum kernel, each CTA: its own P half landed (rescaled tiles)
+  uint64_t ready[STAGES];  // accum kernel, leader: both CTAs' transform warps are done
+  uint64_t empty[STAGES];  // each CTA: the pair's MMAs finished reading the stage
+  uint64_t tfull[2];       // each CTA: its half of an accumulator buffer is complete
+  uint64_t tempty[2];      // leader: both CTAs' epilogues drained the buffer
   uint64_t drain;          // MMA issuer: every UMMA issued has completed
-  uint64_t ring_full[4];   // tile-id ring (dynamic scheduler): id published
-  uint64_t ring_empty[4];  // every consumer role has read the id
-  int ring_id[4];
   uint32_t tmem_base;
   int abort;
 };
-
-// Dynamic tile scheduler. The TMA thread claims tiles from a global counter (one per launch,
-// zeroed by the host) and publishes each id through a 4-slot ring in shared memory; the MMA
-// thread and the epilogue / transform warps read the same sequence. CTAs that start late (the
-// other kernel of the pipeline still holds their SM) simply claim fewer tiles.
-__device__ __forceinline__ int ring_publish(SharedCtl* ctl, int i, int* counter, int n_tiles,
-                                            volatile int* abort) {
-  const int slot = i & 3;
-  if (!mbar_wait(&ctl->ring_empty[slot], ((i >> 2) & 1) ^ 1, abort)) return -1;
-  int tile = atomicAdd(counter, 1);
-  if (tile >= n_tiles) tile = -1;
-  ctl->ring_id[slot] = tile;
-  mbar_arrive(&ctl->ring_full[slot]);
-  return tile;
-}
-
-// One thread's read of ring entry i (then the caller releases the slot with ring_release).
-__device__ __forceinline__ int ring_take(SharedCtl* ctl, int i, volatile int* abort) {
-  const int slot = i & 3;
-  if (!mbar_wait(&ctl->ring_full[slot], (i >> 2) & 1, abort)) return -1;
-  return *reinterpret_cast<volatile int*>(&ctl->ring_id[slot]);
-}
-
-// A warp's read of ring entry i: every lane gets the id (or -1 when done / aborting), lane 0
-// releases the slot.
-__device__ __forceinline__ int ring_take_warp(SharedCtl* ctl, int i, volatile int* abort,
-                                              int lane) {
-  const int slot = i & 3;
-  if (!__all_sync(0xffffffffu, mbar_wait(&ctl->ring_full[slot], (i >> 2) & 1, abort))) return -1;
-  const int tile = *reinterpret_cast<volatile int*>(&ctl->ring_id[slot]);
-  __syncwarp();
-  if (lane == 0) mbar_arrive(&ctl->ring_empty[slot]);
-  return tile;
-}
-
-__device__ __forceinline__ void init_ring(SharedCtl* ctl, int consumers) {
-  for (int r = 0; r < 4; ++r) {
-    mbar_init(&ctl->ring_full[r], 1);
-    mbar_init(&ctl->ring_empty[r], consumers);
-  }
-}
 
 __device__ __forceinline__ uint8_t* aligned_smem(uint8_t* raw) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
 }
 
-// On the way out of the producer: every TMA copy issued must have landed before the CTA
-// releases its shared memory. (stage, phase) is the next slot the producer would have used;
-// the last min(issued, STAGES) slots before it hold the outstanding copies. On the normal path
-// they have all been consumed and each wait returns at once.
+// Write 16 bytes of row r (0..127), 16-byte chunk q (0..7), into a staging buffer laid out as
+// a TMA box of 128 rows x 128 bytes with the 128-byte swizzle (chunk q of row r sits at
+// q ^ (r & 7)): a warp's 32 rows spread over all 8 chunk positions, so every 512-byte warp
+// access takes the minimum 4 shared-memory wavefronts.
+__device__ __forceinline__ void stage_chunk(uint8_t* buf, int r, int q, uint32_t a, uint32_t b,
+                                            uint32_t c, uint32_t d) {
+  *reinterpret_cast<uint4*>(buf + r * 128 + ((q ^ (r & 7)) << 4)) = make_uint4(a, b, c, d);
+}
+
+// Set-up shared by both GEMMs: barriers, TMEM for the pair, cluster-wide visibility.
+__device__ __forceinline__ void pair_setup(SharedCtl* ctl, int warp, int transform_warps) {
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&ctl->full[s], 1);
+      mbar_init(&ctl->afull[s], 1);
+      mbar_init(&ctl->ready[s], 2 * transform_warps > 0 ? 2 * transform_warps : 1);
+      mbar_init(&ctl->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&ctl->tfull[a], 1);
+      mbar_init(&ctl->tempty[a], 2 * EPI_WARPS);  // every epilogue warp of both CTAs
+    }
+    mbar_init(&ctl->drain, 1);
+    ctl->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&ctl->tmem_base, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+}
+
+__device__ __forceinline__ void pair_teardown(SharedCtl* ctl, int warp, uint32_t tmem_base) {
+  tc_fence_before();
+  cluster_sync();  // the peer's shared memory stays alive until the leader's MMAs are done
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+}
+
+// On the way out of the leader's producer: every copy counted on its `full` barriers (both
+// CTAs' halves) must have landed before the pair releases its shared memory. (stage, phase) is
+// the next slot; the last min(issued, STAGES) slots hold the outstanding copies.
 __device__ __forceinline__ void drain_copies(SharedCtl* ctl, int stage, uint32_t phase,
                                              int issued) {
   for (int i = 0; i < STAGES && i < issued; ++i) {
@@ -128,10 +146,9 @@ __device__ __forceinline__ void drain_copies(SharedCtl* ctl, int stage, uint32_t
   }
 }
 
-// On the way out of the MMA issuer: wait until every UMMA it issued has completed, so that no
-// MMA is still writing TMEM when it is released.
+// On the way out of the MMA issuer: wait until every UMMA it issued has completed.
 __device__ __forceinline__ void drain_mmas(SharedCtl* ctl) {
-  umma_commit(&ctl->drain);
+  umma_commit_pair(&ctl->drain);
   mbar_drain(&ctl->drain, 0);
 }
 
@@ -145,85 +162,67 @@ struct LogitsParams {
   int slice_row0;     // first weight row (of this call's range) of the slice
   int cols;           // valid columns of the slice
   int n_col_tiles;    // ceil(cols / BN)
-  int n_row_tiles;    // ceil(n_tokens / BM)
+  int n_parts;        // n_col_tiles * PARTS: statistics records per row
+  int n_pair_rows;    // ceil(n_tokens / PAIR_ROWS)
   long long col_base; // global column id of slice column 0
   int has_ref;        // 0 on the first slice: no reference yet
-  int* tile_counter;  // dynamic scheduler counter of this launch (zeroed by the host)
   const long long* targets;
-  float4* partial;    // [n_tokens][n_col_tiles]: m_t, s_t, t_t, first argmax (int bits)
-  __half* probs;      // [n_grad][ldp]
-  long long ldp;
+  float4* partial;    // [n_tokens][n_parts]: m, s, t, first argmax (int bits) per part
   float* stats;       // [n_tokens][TALM_HEAD_STATS]
 };
 
-__global__ void __launch_bounds__(192, 1)
+// Pair tile t covers rows [pr * 256, +256) x columns [ct * 256, +256) of the slice; the CTA of
+// rank r owns rows pr * 256 + r * 128 + [0, 128) (its TMEM lanes) and loads B rows (weight
+// rows) ct * 256 + r * 128 + [0, 128); the pair's accumulator columns 0..127 come from the
+// leader's B half, 128..255 from the peer's.
+__global__ void __launch_bounds__(LOGITS_THREADS, 1)
     head_logits_kernel(const __grid_constant__ CUtensorMap tm_hidden,
-                       const __grid_constant__ CUtensorMap tm_weight, LogitsParams p) {
+                       const __grid_constant__ CUtensorMap tm_weight,
+                       const __grid_constant__ CUtensorMap tm_probs, LogitsParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = aligned_smem(smem_raw);
-  SharedCtl* ctl = reinterpret_cast<SharedCtl*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* staging = smem + STAGES * STAGE_BYTES;
+  SharedCtl* ctl = reinterpret_cast<SharedCtl*>(staging + STAGING_BYTES);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&ctl->full[s], 1);
-      mbar_init(&ctl->empty[s], 1);
-    }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&ctl->tfull[a], 1);
-      mbar_init(&ctl->tempty[a], 4);  // one arrive per epilogue warp
-    }
-    mbar_init(&ctl->drain, 1);
-    init_ring(ctl, 1 + 4);  // MMA thread + 4 epilogue warps
-    ctl->abort = 0;
-    fence_mbar_init();
     prefetch_tmap(&tm_hidden);
     prefetch_tmap(&tm_weight);
+    if (p.n_grad > 0) prefetch_tmap(&tm_probs);
   }
-  if (warp == 1) {
-    tmem_alloc(&ctl->tmem_base, TMEM_COLS);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
+  pair_setup(ctl, warp, 0);
   const uint32_t tmem_base = ctl->tmem_base;
   volatile int* abort = &ctl->abort;
-  const int n_tiles = p.n_row_tiles * p.n_col_tiles;
+  const int n_tiles = p.n_pair_rows * p.n_col_tiles;
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
 
   if (warp == 0) {
-    if (lane == 0) {  // TMA producer
-      int stage = 0;
+    if (lane == 0) {  // TMA producer (both CTAs): this CTA's halves, counted on the leader
+      int stage = 0, issued = 0;
       uint32_t phase = 0;
-      int issued = 0;
-      for (int i = 0;; ++i) {
-        const int tile = ring_publish(ctl, i, p.tile_counter, n_tiles, abort);
-        if (tile < 0) break;
-        const int rt = tile % p.n_row_tiles, ct = tile / p.n_row_tiles;
+      for (int tile = pair; tile < n_tiles && !*abort; tile += n_pairs) {
+        const int pr = tile % p.n_pair_rows, ct = tile / p.n_pair_rows;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort)) break;
           uint8_t* a = smem + stage * STAGE_BYTES;
-          mbar_arrive_expect_tx(&ctl->full[stage], STAGE_BYTES);
-          tma_load_2d(a, &tm_hidden, &ctl->full[stage], kb * BK, rt * BM);
-          tma_load_2d(a + A_BYTES, &tm_weight, &ctl->full[stage], kb * BK,
-                      p.slice_row0 + ct * BN);
+          const uint32_t lfull = mapa_shared(smem_u32(&ctl->full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&ctl->full[stage], 2 * STAGE_BYTES);
+          tma_load_2d_pair(a, &tm_hidden, lfull, kb * BK, pr * PAIR_ROWS + rank * BM);
+          tma_load_2d_pair(a + A_BYTES, &tm_weight, lfull, kb * BK,
+                           p.slice_row0 + ct * BN + rank * (BN / 2));
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
-      drain_copies(ctl, stage, phase, issued);
+      if (leader) drain_copies(ctl, stage, phase, issued);
     }
   } else if (warp == 1) {
-    if (lane == 0) {  // MMA issuer
-      int stage = 0;
-      uint32_t phase = 0;
-      int acc = 0;
-      uint32_t acc_phase = 0;
-      for (int i = 0;; ++i) {
-        const int tile = ring_take(ctl, i, abort);
-        if (tile < 0) break;
-        mbar_arrive(&ctl->ring_empty[i & 3]);
+    if (lane == 0 && leader) {  // MMA issuer (leader only)
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      for (int tile = pair; tile < n_tiles; tile += n_pairs) {
         if (!mbar_wait(&ctl->tempty[acc], acc_phase ^ 1, abort)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
@@ -235,98 +234,149 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t b = a + A_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            umma_f16(d, smem_desc_sw128(a + k * 32, 16, 1024), smem_desc_sw128(b + k * 32, 16, 1024),
-                     kIdescLogits, (kb | k) != 0);
+            umma_f16_pair(d, smem_desc_sw128(a + k * 32, 16, 1024),
+                          smem_desc_sw128(b + k * 32, 16, 1024), kIdescLogits, (kb | k) != 0);
           }
-          umma_commit(&ctl->empty[stage]);
+          umma_commit_pair(&ctl->empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        umma_commit(&ctl->tfull[acc]);
+        umma_commit_pair(&ctl->tfull[acc]);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
       drain_mmas(ctl);
     }
-  } else {  // epilogue: warps 2..5, TMEM lane quarter = warp % 4
+  } else {  // epilogue: warps 2..9 of both CTAs, TMEM lane quarter = warp % 4
     const int q = warp & 3;
+    const int g = (warp - 2) >> 2;                    // epilogue group: columns g*128..+128
+    const int bar_id = 1 + g;
     const int r_in_tile = q * 32 + lane;
+    const bool elected = (warp - 2) % 4 == 0 && lane == 0;  // the group's TMA-issuing thread
+    uint8_t* buf = staging + g * 16384;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int i = 0;; ++i) {
-      const int tile = ring_take_warp(ctl, i, abort, lane);
-      if (tile < 0) break;
-      const int rt = tile % p.n_row_tiles, ct = tile / p.n_row_tiles;
-      // warp-uniform decision (each lane's wait is bounded, so every lane reaches the vote)
-      if (!__all_sync(0xffffffffu, mbar_wait(&ctl->tfull[acc], acc_phase, abort))) break;
+    for (int tile = pair; tile < n_tiles; tile += n_pairs) {
+      const int pr = tile % p.n_pair_rows, ct = tile / p.n_pair_rows;
+      // CTA-uniform decision among the 4 epilogue warps (named barriers follow; every lane's
+      // wait is bounded, so every thread reaches the vote)
+      const bool landed = mbar_wait(&ctl->tfull[acc], acc_phase, abort);
+      if (named_barrier_or(bar_id, EPI_THREADS, !landed)) break;
       tc_fence_after();
-      const int row = rt * BM + r_in_tile;
+      const int row0 = pr * PAIR_ROWS + rank * BM;  // first row of this CTA's half
+      const int row = row0 + r_in_tile;
       const bool valid_row = row < p.n_tokens;
       const long long tgt = valid_row ? p.targets[row] : -1;
       const long long tile_col0 = p.col_base + static_cast<long long>(ct) * BN;
       const long long tcol_ll = tgt - tile_col0;
-      const int tcol = (tgt >= 0 && tcol_ll >= 0 && tcol_ll < BN) ? static_cast<int>(tcol_ll) : -1;
-      const int ncols = min(BN, p.cols - ct * BN);
+      const int tcol = (tgt >= 0 && tcol_ll >= g * EPI_COLS && tcol_ll < (g + 1) * EPI_COLS)
+                           ? static_cast<int>(tcol_ll) : -1;
+      const int ncols = min(BN, p.cols - ct * BN);  // valid columns of the tile (tile-relative)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      // probabilities leave through the staging buffers by TMA store (64 columns = 16 KiB per
+      // store); CTAs whose rows are all unlabelled (or no gradient) skip them
+      const bool store_p = row0 < p.n_grad;
 
-      // pass 1: max, first argmax, target logit
-      float mx = -INFINITY;
-      int arg = 0;
-      float zt = 0.0f;
-      uint32_t r[32];
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        tmem_ld_32x32b_x32(taddr + c * 32, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int col = c * 32 + j;
-          const float z = round_f16(__uint_as_float(r[j]));
-          if (col < ncols && z > mx) { mx = z; arg = col; }
-          if (col == tcol) zt = z;
-        }
-      }
-      // pass 2: sums and probabilities relative to the row's reference when the tile max stays
-      // within its slack (the common case), else relative to the tile max; the combine kernel
-      // recomputes the same choice from (mx, REF)
+      // Rows with a reference (every slice after the first) take ONE pass over TMEM: logits
+      // rounded to fp16, running max / first argmax / target logit, and s, t, p relative to
+      // REF. If some row's tile max outgrows REF + slack (its reference moves: rare), the CTA
+      // takes a second pass in which those rows use their tile max. The first slice (no
+      // reference yet) takes a max pass, then the sum pass relative to the tile max.
       const float ref = (p.has_ref && valid_row)
                             ? p.stats[static_cast<long long>(row) * TALM_HEAD_STATS + TALM_STAT_REF]
                             : 0.0f;
-      const float base = (p.has_ref && mx <= ref + kRefSlack) ? ref : mx;
-      float s = 0.0f, t = 0.0f;
-      const bool write_p = row < p.n_grad;
-      __half* prow = p.probs + static_cast<long long>(row) * p.ldp + static_cast<long long>(ct) * BN;
-      const float mscaled = base * kLog2e;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      const bool full_tile = ncols >= (g + 1) * EPI_COLS;  // the group's columns all valid
+      // is this warp's target column anywhere in the tile (then the per-element test runs)
+      const bool any_target = __any_sync(0xffffffffu, tcol >= 0);
+      float mx = -INFINITY, zt = 0.0f, s = 0.0f, t = 0.0f;
+      int arg = g * EPI_COLS;
+      uint32_t r[32];
+      // One 32-column chunk: `track` = max / argmax / target, `sum` = s, t and the
+      // probabilities (written to `buf`, 16-byte chunks qbase..qbase+3 of this row). The TMEM
+      // load is warp-collective (.sync.aligned): every lane executes it.
+      auto chunk = [&](int c, bool track, bool sum, float mscaled, uint8_t* buf, int qbase) {
         tmem_ld_32x32b_x32(taddr + c * 32, r);
         tmem_wait_ld();
         uint32_t packed[16];
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
           const int col = c * 32 + j;
-          const float z0 = round_f16(__uint_as_float(r[j]));
-          const float z1 = round_f16(__uint_as_float(r[j + 1]));
-          const float e0 = col < ncols ? ex2(fmaf(z0, kLog2e, -mscaled)) : 0.0f;
-          const float e1 = col + 1 < ncols ? ex2(fmaf(z1, kLog2e, -mscaled)) : 0.0f;
-          s += e0;
-          s += e1;
-          if (col < ncols) t = fmaf(e0, z0, t);
-          if (col + 1 < ncols) t = fmaf(e1, z1, t);
-          packed[j / 2] = pack_half2(e0, e1);
+          // fp16 rounding of the pair as the reference's fp16 GEMM output (one packed cvt)
+          const float2 z = __half22float2(
+              __floats2half2_rn(__uint_as_float(r[j]), __uint_as_float(r[j + 1])));
+          const bool ok0 = full_tile || col < ncols;
+          const bool ok1 = full_tile || col + 1 < ncols;
+          if (track) {
+            if (ok0 && z.x > mx) { mx = z.x; arg = col; }
+            if (ok1 && z.y > mx) { mx = z.y; arg = col + 1; }
+            if (any_target) {
+              if (col == tcol) zt = z.x;
+              if (col + 1 == tcol) zt = z.y;
+            }
+          }
+          if (sum) {
+            const float e0 = ok0 ? ex2(fmaf(z.x, kLog2e, -mscaled)) : 0.0f;
+            const float e1 = ok1 ? ex2(fmaf(z.y, kLog2e, -mscaled)) : 0.0f;
+            s += e0 + e1;
+            t = fmaf(e0, z.x, t);
+            t = fmaf(e1, z.y, t);
+            packed[j / 2] = pack_half2(e0, e1);
+          }
         }
-        if (write_p) {
+        if (sum && buf != nullptr) {
 #pragma unroll
           for (int v = 0; v < 4; ++v)
-            st_v4(prow + c * 32 + v * 8, packed[4 * v], packed[4 * v + 1], packed[4 * v + 2],
-                  packed[4 * v + 3]);
+            stage_chunk(buf, r_in_tile, qbase + v, packed[4 * v], packed[4 * v + 1],
+                        packed[4 * v + 2], packed[4 * v + 3]);
         }
+      };
+      // A pass with sums over the group's columns: 2 blocks of 64 columns, each staged and
+      // stored. `base` per lane; `track` for the single-pass case.
+      auto sum_pass = [&](bool track, float base) {
+        const float mscaled = base * kLog2e;
+#pragma unroll 1
+        for (int kb = g * (EPI_COLS / 64); kb < (g + 1) * (EPI_COLS / 64); ++kb) {
+          if (store_p) {
+            if (elected) bulk_wait_read<0>();  // the group's previous store has read `buf`
+            named_barrier(bar_id, EPI_THREADS);
+          }
+          chunk(2 * kb, track, true, mscaled, store_p ? buf : nullptr, 0);
+          chunk(2 * kb + 1, track, true, mscaled, store_p ? buf : nullptr, 4);
+          if (store_p) {
+            fence_proxy_async_smem();
+            named_barrier(bar_id, EPI_THREADS);
+            if (elected) {
+              tma_store_2d(&tm_probs, buf, ct * BN + kb * 64, row0);
+              bulk_commit();
+            }
+          }
+        }
+      };
+      if (p.has_ref) {
+        s = 0.0f;
+        t = 0.0f;
+        sum_pass(true, ref);
+        const bool jump = mx > ref + kRefSlack;
+        if (named_barrier_or(bar_id, EPI_THREADS, jump)) {
+          // some row's reference moves in the group's columns: they are redone (rows without
+          // a move recompute the same values); earlier stores must land before the new ones
+          if (elected) bulk_wait_all();
+          named_barrier(bar_id, EPI_THREADS);
+          s = 0.0f;
+          t = 0.0f;
+          sum_pass(false, jump ? mx : ref);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = g * (EPI_COLS / 32); c < (g + 1) * (EPI_COLS / 32); ++c)
+          chunk(c, true, false, 0.0f, nullptr, 0);
+        sum_pass(false, mx);
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ctl->tempty[acc]);
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&ctl->tempty[acc]), 0));
       if (valid_row) {
-        p.partial[static_cast<long long>(row) * p.n_col_tiles + ct] =
+        p.partial[static_cast<long long>(row) * p.n_parts + ct * PARTS + g] =
             make_float4(mx, s, t, __int_as_float(static_cast<int>(tile_col0 + arg)));
         if (tcol >= 0 && tcol < ncols) {
           float* st = p.stats + static_cast<long long>(row) * TALM_HEAD_STATS;
@@ -337,12 +387,9 @@ __global__ void __launch_bounds__(192, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (elected) bulk_wait_all();  // every probability store has landed before the CTA leaves
   }
-
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+  pair_teardown(ctl, warp, tmem_base);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -353,7 +400,7 @@ __device__ __forceinline__ void better_arg(float& v, int& i, float v2, int i2) {
 }
 
 __global__ void __launch_bounds__(256) head_combine_kernel(const float4* __restrict__ partial,
-                                                           int n_col_tiles, int n_tokens,
+                                                           int n_parts, int n_tokens,
                                                            int n_grad, int first,
                                                            float* __restrict__ stats,
                                                            float* __restrict__ tile_scale,
@@ -362,7 +409,7 @@ __global__ void __launch_bounds__(256) head_combine_kernel(const float4* __restr
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
   if (row >= n_tokens) return;
-  const float4* pr = partial + static_cast<long long>(row) * n_col_tiles;
+  const float4* pr = partial + static_cast<long long>(row) * n_parts;
   float* st = stats + static_cast<long long>(row) * TALM_HEAD_STATS;
   // every lane reads the running statistics before lane 0 overwrites them
   const float ref = first ? 0.0f : st[TALM_STAT_REF];
@@ -374,7 +421,7 @@ __global__ void __launch_bounds__(256) head_combine_kernel(const float4* __restr
   // the slice's max and first argmax
   float M = -INFINITY, bv = -INFINITY;
   int bi = 0x7fffffff;
-  for (int j = lane; j < n_col_tiles; j += 32) {
+  for (int j = lane; j < n_parts; j += 32) {
     const float4 v = pr[j];
     M = fmaxf(M, v.x);
     better_arg(bv, bi, v.x, __float_as_int(v.w));
@@ -392,8 +439,8 @@ __global__ void __launch_bounds__(256) head_combine_kernel(const float4* __restr
   const float ref_new = jump ? m_new : ref;
   // tile sums were taken relative to base_j = (has ref and m_j <= ref + slack) ? ref : m_j
   float S = 0.0f, T = 0.0f;
-  float* sc = tile_scale + static_cast<long long>(row) * n_col_tiles;
-  for (int j = lane; j < n_col_tiles; j += 32) {
+  float* sc = tile_scale + static_cast<long long>(row) * n_parts;
+  for (int j = lane; j < n_parts; j += 32) {
     const float4 v = pr[j];
     const float base = (!first && v.x <= ref + kRefSlack) ? ref : v.x;
     const float w = ex2((base - ref_new) * kLog2e);
@@ -431,103 +478,100 @@ struct AccumParams {
   int hidden;
   int k_blocks;      // slice columns / BK (padded slice: a multiple of BN / BK)
   int slice_row0;    // first weight row of the slice
-  int n_col_tiles;   // tiles of the slice (for the scale table)
-  int n_row_tiles;   // ceil(n_grad / BM)
+  int n_parts;       // statistics records per row of the slice (the scale table's stride)
+  int n_pair_rows;   // ceil(n_grad / PAIR_ROWS)
   int n_h_tiles;     // ceil(hidden / BN)
   int first;
-  const float* tile_scale;  // [n_grad][n_col_tiles]
+  const float* tile_scale;  // [n_grad][n_parts]: factor per 128 columns
   const float* alpha;       // [n_grad]
-  const int* block_jump;    // [n_row_tiles]: some row of the block moved its reference
-  int* tile_counter;        // dynamic scheduler counter of this launch (zeroed by the host)
+  const int* block_jump;    // [ceil(n_grad / BM) + 1]: some row of the 128-row block moved its REF
   float* acc;               // [n_grad][hidden]
 };
 
-__global__ void __launch_bounds__(320, 1)
+// Pair tile t covers labelled rows [pr * 256, +256) x hidden columns [ht * 256, +256); the CTA
+// of rank r owns rows pr * 256 + r * 128 + [0, 128) and loads the hidden columns
+// ht * 256 + r * 128 + [0, 128) of W (two 64-wide MN-major boxes per stage).
+__global__ void __launch_bounds__(ACCUM_THREADS, 1)
     head_accum_kernel(const __grid_constant__ CUtensorMap tm_probs,
-                      const __grid_constant__ CUtensorMap tm_weight_mn, AccumParams p) {
+                      const __grid_constant__ CUtensorMap tm_weight_mn,
+                      const __grid_constant__ CUtensorMap tm_acc, AccumParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = aligned_smem(smem_raw);
-  SharedCtl* ctl = reinterpret_cast<SharedCtl*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* staging = smem + STAGES * STAGE_BYTES;
+  SharedCtl* ctl = reinterpret_cast<SharedCtl*>(staging + STAGING_BYTES);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&ctl->full[s], 1);
-      mbar_init(&ctl->ready[s], 4);  // one arrive per transform warp
-      mbar_init(&ctl->empty[s], 1);
-    }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&ctl->tfull[a], 1);
-      mbar_init(&ctl->tempty[a], 4);  // one arrive per epilogue warp
-    }
-    mbar_init(&ctl->drain, 1);
-    init_ring(ctl, 1 + 4 + 4);  // MMA thread + 4 epilogue warps + 4 transform warps
-    ctl->abort = 0;
-    fence_mbar_init();
     prefetch_tmap(&tm_probs);
     prefetch_tmap(&tm_weight_mn);
+    prefetch_tmap(&tm_acc);
   }
-  if (warp == 1) {
-    tmem_alloc(&ctl->tmem_base, TMEM_COLS);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
+  pair_setup(ctl, warp, 4);
   const uint32_t tmem_base = ctl->tmem_base;
   volatile int* abort = &ctl->abort;
-  const int n_tiles = p.n_row_tiles * p.n_h_tiles;
+  const int n_tiles = p.n_pair_rows * p.n_h_tiles;
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+  // A pair tile is rescaled when either of its 128-row blocks moved its reference; both CTAs
+  // and every role read the same two flags.
+  auto transformed = [&](int pr) {
+    return (__ldg(p.block_jump + 2 * pr) | __ldg(p.block_jump + 2 * pr + 1)) != 0;
+  };
 
   if (warp == 0) {
-    if (lane == 0) {  // TMA producer
-      int stage = 0;
-      uint32_t phase = 0;
-      int issued = 0;
-      for (int i = 0;; ++i) {
-        const int tile = ring_publish(ctl, i, p.tile_counter, n_tiles, abort);
-        if (tile < 0) break;
-        const int ht = tile % p.n_h_tiles, rt = tile / p.n_h_tiles;
+    if (lane == 0) {  // TMA producer (both CTAs)
+      int stage = 0, issued = 0;
+      uint32_t phase = 0, afull_phase = 0, issued_afull = 0;
+      for (int tile = pair; tile < n_tiles && !*abort; tile += n_pairs) {
+        const int ht = tile % p.n_h_tiles, pr = tile / p.n_h_tiles;
+        const bool tf = transformed(pr);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort)) break;
           uint8_t* a = smem + stage * STAGE_BYTES;
-          mbar_arrive_expect_tx(&ctl->full[stage], STAGE_BYTES);
-          tma_load_2d(a, &tm_probs, &ctl->full[stage], kb * BK, rt * BM);
+          const uint32_t lfull = mapa_shared(smem_u32(&ctl->full[stage]), 0);
+          const int row0 = pr * PAIR_ROWS + rank * BM;
+          if (tf) {
+            // P goes to this CTA's transform warps first; only W is counted on the leader
+            mbar_arrive_expect_tx(&ctl->afull[stage], A_BYTES);
+            tma_load_2d(a, &tm_probs, &ctl->afull[stage], kb * BK, row0);
+            afull_phase ^= 1u << stage;
+            issued_afull |= 1u << stage;
+            if (leader) mbar_arrive_expect_tx(&ctl->full[stage], 2 * B_BYTES);
+          } else {
+            if (leader) mbar_arrive_expect_tx(&ctl->full[stage], 2 * STAGE_BYTES);
+            tma_load_2d_pair(a, &tm_probs, lfull, kb * BK, row0);
+          }
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j)
-            tma_load_2d(a + A_BYTES + j * (64 * BK * 2), &tm_weight_mn, &ctl->full[stage],
-                        ht * BN + j * 64, p.slice_row0 + kb * BK);
+          for (int j = 0; j < BN / 2 / 64; ++j)
+            tma_load_2d_pair(a + A_BYTES + j * (64 * BK * 2), &tm_weight_mn, lfull,
+                             ht * BN + rank * (BN / 2) + j * 64, p.slice_row0 + kb * BK);
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
-      drain_copies(ctl, stage, phase, issued);
+      // this CTA's own P copies (rescaled tiles) complete on its afull barriers: let the last
+      // one of each stage land before the CTA can leave
+      for (int st = 0; st < STAGES; ++st)
+        if (issued_afull & (1u << st)) mbar_drain(&ctl->afull[st], ((afull_phase >> st) & 1u) ^ 1u);
+      if (leader) drain_copies(ctl, stage, phase, issued);
     }
   } else if (warp == 1) {
-    if (lane == 0) {  // MMA issuer
-      int stage = 0;
-      uint32_t phase = 0;
-      int acc = 0;
-      uint32_t acc_phase = 0;
+    if (lane == 0 && leader) {  // MMA issuer (leader only)
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
       uint32_t ready_phase = 0;  // bit s: parity of the next phase of ready[s]
-      for (int i = 0;; ++i) {
-        const int tile = ring_take(ctl, i, abort);
-        if (tile < 0) break;
-        mbar_arrive(&ctl->ring_empty[i & 3]);
+      for (int tile = pair; tile < n_tiles; tile += n_pairs) {
         if (!mbar_wait(&ctl->tempty[acc], acc_phase ^ 1, abort)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
-        // tiles whose rows all kept their reference need no rescaling: the MMA consumes the
-        // TMA'd stage directly; otherwise it waits for the transform warps
-        const bool transformed = __ldg(p.block_jump + tile / p.n_h_tiles) != 0;
+        const bool tf = transformed(tile / p.n_h_tiles);
         bool ok = true;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
-          bool landed;
-          if (transformed) {
+          bool landed = mbar_wait(&ctl->full[stage], phase, abort);
+          if (landed && tf) {
             landed = mbar_wait(&ctl->ready[stage], (ready_phase >> stage) & 1u, abort);
             ready_phase ^= 1u << stage;
-          } else {
-            landed = mbar_wait(&ctl->full[stage], phase, abort);
           }
           if (!landed) { ok = false; break; }
           tc_fence_after();
@@ -535,46 +579,43 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t b = a + A_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            // A: K-major rows of 128 B, +32 B per 16 K. B: MN-major, 64-wide hidden groups of
-            // BK rows x 128 B (LBO = 8 KiB), 16 K-rows = +2 KiB.
-            umma_f16(d, smem_desc_sw128(a + k * 32, 16, 1024),
-                     smem_desc_sw128(b + k * 2048, 64 * BK * 2, 1024), kIdescAccum,
-                     (kb | k) != 0);
+            // A: K-major rows of 128 B, +32 B per 16 K. B: MN-major, two 64-wide hidden groups
+            // of BK rows x 128 B (LBO = 8 KiB), 16 K-rows = +2 KiB.
+            umma_f16_pair(d, smem_desc_sw128(a + k * 32, 16, 1024),
+                          smem_desc_sw128(b + k * 2048, 64 * BK * 2, 1024), kIdescAccum,
+                          (kb | k) != 0);
           }
-          umma_commit(&ctl->empty[stage]);
+          umma_commit_pair(&ctl->empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        umma_commit(&ctl->tfull[acc]);
+        umma_commit_pair(&ctl->tfull[acc]);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
       drain_mmas(ctl);
     }
-  } else if (warp >= 6) {  // transform: p -> p * exp(m_t - m_new), one row per thread
-    const int r_in_tile = (warp - 6) * 32 + lane;
+  } else if (warp >= 2 + EPI_WARPS) {  // transform (both CTAs): p -> p * exp(base - REF_new)
+    const int r_in_tile = (warp - 2 - EPI_WARPS) * 32 + lane;
     int stage = 0;
-    uint32_t phase = 0;
-    for (int i = 0;; ++i) {
-      const int tile = ring_take_warp(ctl, i, abort, lane);
-      if (tile < 0) break;
-      const int rt = tile / p.n_h_tiles;
-      if (__ldg(p.block_jump + rt) == 0) {  // the MMA consumes these stages untouched
-        const int adv = p.k_blocks % STAGES;
-        phase ^= static_cast<uint32_t>((p.k_blocks / STAGES) & 1);
-        if (stage + adv >= STAGES) phase ^= 1;
-        stage = (stage + adv) % STAGES;
+    uint32_t afull_phase = 0;  // bit s: parity of the next phase of afull[s]
+    for (int tile = pair; tile < n_tiles; tile += n_pairs) {
+      const int pr = tile / p.n_h_tiles;
+      if (!transformed(pr)) {  // the MMA consumes these stages untouched
+        stage = (stage + p.k_blocks) % STAGES;
         continue;
       }
-      const int row = min(rt * BM + r_in_tile, p.n_grad - 1);
-      const float* sc_row = p.tile_scale + static_cast<long long>(row) * p.n_col_tiles;
+      const int row = min(pr * PAIR_ROWS + static_cast<int>(rank) * BM + r_in_tile, p.n_grad - 1);
+      const float* sc_row = p.tile_scale + static_cast<long long>(row) * p.n_parts;
       bool ok = true;
       for (int kb = 0; kb < p.k_blocks; ++kb) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&ctl->full[stage], phase, abort))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&ctl->afull[stage], (afull_phase >> stage) & 1u,
+                                                abort))) {
           ok = false;
           break;
         }
-        const float sc = __ldg(sc_row + (kb * BK) / BN);
+        afull_phase ^= 1u << stage;
+        const float sc = __ldg(sc_row + (kb * BK) / EPI_COLS);
         uint4* line = reinterpret_cast<uint4*>(smem + stage * STAGE_BYTES + r_in_tile * 128);
         // Visit the row's 16-byte chunks in logical order: logical chunk c sits at c ^ (row & 7)
         // (128-byte swizzle), so the 32 lanes of a warp spread over all 8 chunk positions and
@@ -594,74 +635,82 @@ __global__ void __launch_bounds__(320, 1)
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&ctl->ready[stage]);
-        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&ctl->ready[stage]), 0));
+        if (++stage == STAGES) stage = 0;
       }
       if (!ok) break;
     }
-  } else {  // epilogue: warps 2..5
+  } else {  // epilogue: warps 2..9 of both CTAs
     const int q = warp & 3;
+    const int g = (warp - 2) >> 2;                    // epilogue group: hidden columns g*128..
+    const int bar_id = 1 + g;
     const int r_in_tile = q * 32 + lane;
+    const bool elected = (warp - 2) % 4 == 0 && lane == 0;  // the group's TMA-issuing thread
+    uint8_t* buf = staging + g * 16384;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int i = 0;; ++i) {
-      const int tile = ring_take_warp(ctl, i, abort, lane);
-      if (tile < 0) break;
-      const int ht = tile % p.n_h_tiles, rt = tile / p.n_h_tiles;
-      // warp-uniform decision (each lane's wait is bounded, so every lane reaches the vote)
-      if (!__all_sync(0xffffffffu, mbar_wait(&ctl->tfull[acc], acc_phase, abort))) break;
+    for (int tile = pair; tile < n_tiles; tile += n_pairs) {
+      const int ht = tile % p.n_h_tiles, pr = tile / p.n_h_tiles;
+      // CTA-uniform decision among the 4 epilogue warps (named barriers follow)
+      const bool landed = mbar_wait(&ctl->tfull[acc], acc_phase, abort);
+      if (named_barrier_or(bar_id, EPI_THREADS, !landed)) break;
       tc_fence_after();
-      const int row = rt * BM + r_in_tile;
+      const int row0 = pr * PAIR_ROWS + static_cast<int>(rank) * BM;
+      const int row = row0 + r_in_tile;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      const float al = (row < p.n_grad && !p.first) ? p.alpha[row] : 0.0f;
-      float* arow = p.acc + static_cast<long long>(row) * p.hidden + ht * BN;
-      uint32_t r[32];
+      // acc = alpha * acc + D. Rows that kept their reference have alpha = 1: D is added by
+      // TMA reduce-add (no read of acc at all). A row whose reference moved in this slice has
+      // its acc slice rescaled here first; the first slice stores D.
+      if (!p.first && row < p.n_grad) {
+        const float al = p.alpha[row];
+        if (al != 1.0f) {
+          float4* arow = reinterpret_cast<float4*>(p.acc + static_cast<long long>(row) * p.hidden +
+                                                   ht * BN + g * EPI_COLS);
+          const int n4 = max(0, min(EPI_COLS, p.hidden - ht * BN - g * EPI_COLS)) / 4;
+          for (int v = 0; v < n4; ++v) {
+            float4 o = arow[v];
+            o.x *= al;
+            o.y *= al;
+            o.z *= al;
+            o.w *= al;
+            arow[v] = o;
+          }
+          fence_proxy_async_global();  // the scaled values precede the reduce-adds below
+        }
+      }
+      const bool any_rows = row0 < p.n_grad;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = g * (EPI_COLS / 32); c < (g + 1) * (EPI_COLS / 32); ++c) {
+        uint32_t r[32];
         tmem_ld_32x32b_x32(taddr + c * 32, r);
         tmem_wait_ld();
-        const int h0 = ht * BN + c * 32;
-        if (row < p.n_grad) {
-          if (h0 + 32 <= p.hidden) {
-            float4* dst = reinterpret_cast<float4*>(arow + c * 32);
+        if (any_rows && ht * BN + c * 32 < p.hidden) {
+          if (elected) bulk_wait_read<0>();  // the group's previous reduce has read `buf`
+          named_barrier(bar_id, EPI_THREADS);
 #pragma unroll
-            for (int v = 0; v < 8; ++v) {
-              float4 o;
-              if (p.first) {
-                o = make_float4(0.f, 0.f, 0.f, 0.f);
-              } else {
-                o = dst[v];
-              }
-              o.x = fmaf(o.x, al, __uint_as_float(r[4 * v + 0]));
-              o.y = fmaf(o.y, al, __uint_as_float(r[4 * v + 1]));
-              o.z = fmaf(o.z, al, __uint_as_float(r[4 * v + 2]));
-              o.w = fmaf(o.w, al, __uint_as_float(r[4 * v + 3]));
-              dst[v] = o;
+          for (int v = 0; v < 8; ++v)
+            stage_chunk(buf, r_in_tile, v, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+          fence_proxy_async_smem();
+          named_barrier(bar_id, EPI_THREADS);
+          if (elected) {
+            if (p.first) {
+              tma_store_2d(&tm_acc, buf, ht * BN + c * 32, row0);
+            } else {
+              tma_reduce_add_2d(&tm_acc, buf, ht * BN + c * 32, row0);
             }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (h0 + j < p.hidden) {
-                float* dst = arow + c * 32 + j;
-                const float old = p.first ? 0.0f : *dst;
-                *dst = fmaf(old, al, __uint_as_float(r[j]));
-              }
-            }
+            bulk_commit();
           }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ctl->tempty[acc]);
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&ctl->tempty[acc]), 0));
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (elected) bulk_wait_all();  // every accumulator update has landed before the CTA leaves
   }
-
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+  pair_teardown(ctl, warp, tmem_base);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -778,7 +827,7 @@ inline int64_t chunk_cols(int64_t vocab_cols, int64_t vocab_chunk) {
 Workspace layout(int64_t n_tokens, int64_t n_grad, int64_t vocab_cols, int64_t vocab_chunk,
                  uint8_t* base) {
   const int64_t chunk = chunk_cols(vocab_cols, vocab_chunk);
-  const int64_t tiles = chunk / BN;
+  const int64_t tiles = chunk / BN * PARTS;  // statistics records per row and slice
   const int64_t n_slices = (vocab_cols + chunk - 1) / chunk;
   const int n_buf = n_slices > 1 ? 2 : 1;
   Workspace w;
@@ -852,6 +901,35 @@ int set_attrs() {
   return TALM_OK;
 }
 
+// Launch one of the pair GEMMs: clusters of 2 CTAs, one pair per 2 SMs at most, never more
+// pairs than tiles.
+template <class Params>
+int launch_pair_kernel(void (*kernel)(CUtensorMap, CUtensorMap, CUtensorMap, Params),
+                       int threads, int n_tiles, const CUtensorMap& m0, const CUtensorMap& m1,
+                       const CUtensorMap& m2, const Params& params, cudaStream_t stream,
+                       int max_pairs) {
+  int pairs = n_tiles < max_pairs ? n_tiles : max_pairs;
+  if (pairs < 1) pairs = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, m0, m1, m2, params);
+  if (e != cudaSuccess) return set_error(TALM_ECUDA, "pair kernel launch: %s", cudaGetErrorString(e));
+  return TALM_OK;
+}
+
+// Pairs that fit on the GPU at once (one CTA per SM: shared memory and TMEM are taken whole).
+int max_pairs_of(int sms) { return sms / 2 > 0 ? sms / 2 : 1; }
+
 }  // namespace head
 }  // namespace talm
 
@@ -901,9 +979,12 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
   CUtensorMap tm_hidden, tm_weight, tm_weight_mn;
   st = talm_make_tmap_2d_f16(&tm_hidden, hidden, hidden_size, n_tokens, ld_hidden, BK, BM);
   if (st == TALM_OK)
-    st = talm_make_tmap_2d_f16(&tm_weight, weight, hidden_size, vocab_cols, ld_weight, BK, BN);
+    st = talm_make_tmap_2d_f16(&tm_weight, weight, hidden_size, vocab_cols, ld_weight, BK, BN / 2);
   if (st == TALM_OK && n_grad > 0)
     st = talm_make_tmap_2d_f16(&tm_weight_mn, weight, hidden_size, vocab_cols, ld_weight, 64, BK);
+  CUtensorMap tm_acc = tm_hidden;
+  if (st == TALM_OK && n_grad > 0)
+    st = talm_make_tmap_2d_f32(&tm_acc, acc, hidden_size, n_grad, hidden_size, 32, BM);
   if (st != TALM_OK) return st;
 
   const int64_t n_slices = (vocab_cols + chunk - 1) / chunk;
@@ -912,9 +993,10 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
   // The accumulator GEMM goes to the side stream (overlapping the next slice's logits GEMM)
   // only when it has fewer tiles than the GPU has SMs; a GEMM that fills the GPU on its own
   // gains nothing from sharing it and runs in order on the caller's stream.
-  const int64_t grad_tiles = ((n_grad + BM - 1) / BM) * ((hidden_size + BN - 1) / BN);
+  const int64_t grad_pairs =
+      ((n_grad + PAIR_ROWS - 1) / PAIR_ROWS) * ((hidden_size + BN - 1) / BN);
   SidePipe* pipe = nullptr;
-  if (n_grad > 0 && n_slices > 1 && grad_tiles < sms && (st = side_pipe(&pipe)) != TALM_OK)
+  if (n_grad > 0 && n_slices > 1 && grad_pairs < sms / 2 && (st = side_pipe(&pipe)) != TALM_OK)
     return st;
 
   if (cudaMemsetAsync(stats, 0, sizeof(float) * TALM_HEAD_STATS * n_tokens, stream) != cudaSuccess)
@@ -926,7 +1008,8 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
     return check_launch("flag memset");
 
   const int k_blocks = static_cast<int>((hidden_size + BK - 1) / BK);
-  const int n_row_tiles = static_cast<int>((n_tokens + BM - 1) / BM);
+  const int n_pair_rows = static_cast<int>((n_tokens + PAIR_ROWS - 1) / PAIR_ROWS);
+  const int max_pairs = max_pairs_of(sms);
   for (int64_t k = 0; k < n_slices; ++k) {
     const int64_t s0 = k * chunk;
     const int buf = static_cast<int>(k & 1);
@@ -943,26 +1026,28 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
     lp.slice_row0 = static_cast<int>(s0);
     lp.cols = cols;
     lp.n_col_tiles = n_col_tiles;
-    lp.n_row_tiles = n_row_tiles;
+    lp.n_parts = n_col_tiles * PARTS;
+    lp.n_pair_rows = n_pair_rows;
     lp.col_base = vocab_col0 + s0;
     lp.has_ref = k != 0;
-    lp.tile_counter = ws.counters + 2 * k;
     lp.targets = reinterpret_cast<const long long*>(targets);
     lp.partial = ws.partial;
-    lp.probs = ws.probs[buf];
-    lp.ldp = chunk;
     lp.stats = stats;
-    const int tiles = n_row_tiles * n_col_tiles;
+    CUtensorMap tm_probs = tm_hidden;  // unused when no probabilities are stored
+    if (n_grad > 0 &&
+        (st = talm_make_tmap_2d_f16(&tm_probs, ws.probs[buf], chunk, n_grad, chunk, 64, BM)) !=
+            TALM_OK)
+      return st;
     {
       LaunchTimer timer(TALM_KERNEL_HEAD_LOGITS, stream);
-      head_logits_kernel<<<tiles < sms ? tiles : sms, 192, SMEM_BYTES, stream>>>(
-          tm_hidden, tm_weight, lp);
+      st = launch_pair_kernel(head_logits_kernel, LOGITS_THREADS, n_pair_rows * n_col_tiles, tm_hidden,
+                              tm_weight, tm_probs, lp, stream, max_pairs);
     }
-    if ((st = check_launch("head logits kernel")) != TALM_OK) return st;
+    if (st != TALM_OK) return st;
     {
       LaunchTimer timer(TALM_KERNEL_HEAD_COMBINE, stream);
       head_combine_kernel<<<static_cast<int>((n_tokens + 7) / 8), 256, 0, stream>>>(
-          ws.partial, n_col_tiles, static_cast<int>(n_tokens), static_cast<int>(n_grad), k == 0,
+          ws.partial, n_col_tiles * PARTS, static_cast<int>(n_tokens), static_cast<int>(n_grad), k == 0,
           stats, ws.tile_scale[buf], ws.alpha[buf], slice_jump);
     }
     if ((st = check_launch("head combine kernel")) != TALM_OK) return st;
@@ -972,31 +1057,26 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
       if (pipe && (cudaEventRecord(pipe->combined[buf], stream) != cudaSuccess ||
                    cudaStreamWaitEvent(pipe->stream, pipe->combined[buf], 0) != cudaSuccess))
         return check_launch("fork to the side stream");
-      CUtensorMap tm_probs;
-      if ((st = talm_make_tmap_2d_f16(&tm_probs, ws.probs[buf], chunk, n_grad, chunk, BK, BM)) !=
-          TALM_OK)
-        return st;
+
       AccumParams ap;
       ap.n_grad = static_cast<int>(n_grad);
       ap.hidden = static_cast<int>(hidden_size);
       ap.k_blocks = n_col_tiles * (BN / BK);
       ap.slice_row0 = static_cast<int>(s0);
-      ap.n_col_tiles = n_col_tiles;
-      ap.n_row_tiles = static_cast<int>((n_grad + BM - 1) / BM);
+      ap.n_parts = n_col_tiles * PARTS;
+      ap.n_pair_rows = static_cast<int>((n_grad + PAIR_ROWS - 1) / PAIR_ROWS);
       ap.n_h_tiles = static_cast<int>((hidden_size + BN - 1) / BN);
       ap.first = k == 0;
       ap.tile_scale = ws.tile_scale[buf];
       ap.alpha = ws.alpha[buf];
       ap.block_jump = slice_jump;
-      ap.tile_counter = ws.counters + 2 * k + 1;
       ap.acc = acc;
-      const int atiles = ap.n_row_tiles * ap.n_h_tiles;
       {
         LaunchTimer timer(TALM_KERNEL_HEAD_ACCUM, acc_stream);
-        head_accum_kernel<<<atiles < sms ? atiles : sms, 320, SMEM_BYTES, acc_stream>>>(
-            tm_probs, tm_weight_mn, ap);
+        st = launch_pair_kernel(head_accum_kernel, ACCUM_THREADS, ap.n_pair_rows * ap.n_h_tiles, tm_probs,
+                                tm_weight_mn, tm_acc, ap, acc_stream, max_pairs);
       }
-      if ((st = check_launch("head accumulator kernel")) != TALM_OK) return st;
+      if (st != TALM_OK) return st;
       if (pipe && cudaEventRecord(pipe->drained[buf], pipe->stream) != cudaSuccess)
         return check_launch("side stream event");
     }
