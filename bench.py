@@ -66,6 +66,8 @@ def parse_args():
                    help="headline only (no c2 / nf4 / cpu baseline)")
     p.add_argument("--only-nf4", action="store_true",
                    help="the NF4 part alone (profiling runs); prints its JSON object")
+    p.add_argument("--nf4-layers", type=int, default=N_LAYERS,
+                   help="layers in the config-3 sweep (fewer: a small case for ncu captures)")
     return p.parse_args()
 
 
@@ -324,7 +326,7 @@ def run_head_e2e(world, rank, steps, warmup, hidden, weight, targets):
     return ms / steps, h2d, 4 * world
 
 
-def run_nf4(world, rank, steps, warmup):
+def run_nf4(world, rank, steps, warmup, n_layers=N_LAYERS):
     """Config 3 (28 layers, double-quantised, layer-sharded) and, on one GPU, config 1."""
     from talm_b200 import _lib
     from talm_b200.nf4_dequant import nf4_dequantize
@@ -332,7 +334,7 @@ def run_nf4(world, rank, steps, warmup):
     from talm_b200.vocab_parallel import shard_bounds
 
     res = {}
-    l0, nl = shard_bounds(N_LAYERS, world, rank)
+    l0, nl = shard_bounds(n_layers, world, rank)
     layers = [nf4_layer(l0 + i, "cuda", True) for i in range(nl)]
     levels = _levels(torch.device("cuda"))
     n_rows = layers[0]["n"] // 64 if layers else 0
@@ -346,10 +348,10 @@ def run_nf4(world, rank, steps, warmup):
         sweep()
     ms = timed(sweep, steps, world)
     prof = profile_kernels(sweep, steps)
-    total_bytes = N_LAYERS * 117_736_832
+    total_bytes = n_layers * 117_736_832
     k_ms, k_n = prof["nf4"]
-    res["c3"] = {"workload": "28 Qwen2.5-1.5B layers, double-quantised absmax, one grouped "
-                             "launch per layer, layers sharded contiguously over the ranks",
+    res["c3"] = {"workload": f"{n_layers} Qwen2.5-1.5B layers, double-quantised absmax, one "
+                             "grouped launch per layer, layers sharded contiguously over the ranks",
                  "GB_per_s": total_bytes / (ms / steps) / 1e6, "ms_per_sweep": ms / steps,
                  "bytes_per_sweep": total_bytes,
                  "kernel_us_per_layer": 1000 * k_ms / max(k_n, 1)}
@@ -488,7 +490,7 @@ def ours(args, world, rank, local):
                           / (c2["ms_per_step"] / 1000) / 1e12 / pk["bf16_tflops"],
                           "kernels_ms_per_step": {k: v[0] / args.steps for k, v in k2.items()
                                                   if v[1]}}
-        nf4 = run_nf4(world, rank, args.steps, args.warmup)
+        nf4 = run_nf4(world, rank, args.steps, args.warmup, args.nf4_layers)
         if "c1" in nf4:
             nf4["c1"]["roofline"] = {"bound": "hbm", "achieved": nf4["c1"]["kernel_GB_per_s"],
                                      "peak": pk["hbm_gbs"], "unit": "GB/s",
@@ -547,7 +549,7 @@ def main():
     world, rank, local = init_dist(args.gpus)
     try:
         if args.only_nf4:
-            line = {"nf4": run_nf4(world, rank, args.steps, args.warmup)}
+            line = {"nf4": run_nf4(world, rank, args.steps, args.warmup, args.nf4_layers)}
         else:
             line = ours(args, world, rank, local)
         if rank == 0:

@@ -13,13 +13,15 @@
 //      only [rows, chunk] buffer of the head; it stays in L2 at the configured sizes).
 //   2. head_combine_kernel: one warp per row merges the slice's tile statistics with the running
 //      statistics of the earlier slices (log-sum-exp merge), and for labelled rows writes
-//      per-tile factors exp(m_t - m_new) and the accumulator rescale alpha = exp(m_old - m_new)
-//      (the online-softmax rescale of solution/fused_head.py:170-177).
-//   3. head_accum_kernel (tcgen05, persistent): acc[128 rows, 256 hidden] = alpha * acc +
-//      P' W_slice, K = slice columns. P arrives by TMA; four transform warps rescale it in shared
-//      memory to p * exp(m_t - m_new) (so the GEMM operand equals fp16(exp(z - m_new)), the
-//      reference's in-place softmax weights) before the MMA warp consumes the stage. W_slice is
-//      read MN-major (hidden contiguous) straight from the weight rows.
+//      per-tile factors exp(m_t - m_new); a row whose reference moved has its acc row multiplied
+//      by alpha = exp(m_old - m_new) here (the online-softmax rescale of
+//      solution/fused_head.py:170-177).
+//   3. head_accum_kernel (tcgen05, persistent): acc[256 rows, 256 hidden] += P' W_slice,
+//      K = slice columns, by TMA reduce-add into an acc that starts at zero. P arrives by TMA;
+//      four transform warps rescale it in shared memory to p * exp(m_t - m_new) (so the GEMM
+//      operand equals fp16(exp(z - m_new)), the reference's in-place softmax weights) before the
+//      MMA warp consumes the stage. W_slice is read MN-major (hidden contiguous) straight from
+//      the weight rows. The last, partial wave of tiles is split along K over all CTA pairs.
 //
 // A last launch (head_finalize_kernel) turns the statistics into loss / entropy / correctness
 // and the accumulator into dH = acc / s - fp16(W[target]) (fused_head.py:111-125, :160-169),
@@ -62,6 +64,8 @@ constexpr float kLog2e = 1.4426950408889634f;
 // Slack of the lazy reference: a row's probabilities and accumulator stay relative to REF while
 // its running max is at most REF + kRefSlack, so p = exp(z - REF) <= e^8 (fits fp16).
 constexpr float kRefSlack = 8.0f;
+// Smallest K range (in BK blocks) of a split accumulator tile piece.
+constexpr int kMinSplitBlocks = 8;
 
 // M = 256 across the CTA pair, N = 256 (128 columns of B in each CTA's shared memory)
 constexpr uint32_t kIdescLogits = idesc_f16_f32(PAIR_ROWS, BN, false, false);  // A, B K-major
@@ -404,8 +408,8 @@ __global__ void __launch_bounds__(256) head_combine_kernel(const float4* __restr
                                                            int n_grad, int first,
                                                            float* __restrict__ stats,
                                                            float* __restrict__ tile_scale,
-                                                           float* __restrict__ alpha,
-                                                           int* __restrict__ block_jump) {
+                                                           int* __restrict__ block_jump,
+                                                           float* __restrict__ acc, int hidden) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
   if (row >= n_tokens) return;
@@ -463,15 +467,25 @@ __global__ void __launch_bounds__(256) head_combine_kernel(const float4* __restr
       st[TALM_STAT_BEST] = bv;
       st[TALM_STAT_IDX] = __int_as_float(bi);
     }
-    if (row < n_grad) {
-      alpha[row] = a;
-      if (jump) atomicOr(block_jump + row / BM, 1);
+    if (row < n_grad && jump) atomicOr(block_jump + row / BM, 1);
+  }
+  // acc = alpha * acc for a row whose reference moved (alpha = 1 for every other row); the
+  // earlier slices' accumulator GEMMs precede this launch, the current slice's follows it
+  if (!first && jump && row < n_grad && acc != nullptr) {
+    float4* arow = reinterpret_cast<float4*>(acc + static_cast<long long>(row) * hidden);
+    for (int v = lane; v < hidden / 4; v += 32) {
+      float4 o = arow[v];
+      o.x *= a;
+      o.y *= a;
+      o.z *= a;
+      o.w *= a;
+      arow[v] = o;
     }
   }
 }
 
 // ------------------------------------------------------------------------------------------
-// 3. accumulator GEMM: acc = alpha * acc + P' W_slice
+// 3. accumulator GEMM: acc += P' W_slice (acc starts at zero; jump rows rescaled by combine)
 // ------------------------------------------------------------------------------------------
 struct AccumParams {
   int n_grad;
@@ -481,12 +495,43 @@ struct AccumParams {
   int n_parts;       // statistics records per row of the slice (the scale table's stride)
   int n_pair_rows;   // ceil(n_grad / PAIR_ROWS)
   int n_h_tiles;     // ceil(hidden / BN)
-  int first;
+  int split;         // 1: the tiles of the last, partial wave are split along K over all pairs
   const float* tile_scale;  // [n_grad][n_parts]: factor per 128 columns
-  const float* alpha;       // [n_grad]
   const int* block_jump;    // [ceil(n_grad / BM) + 1]: some row of the 128-row block moved its REF
-  float* acc;               // [n_grad][hidden]
 };
+
+// Work unit u of pair `pair`: K-blocks [kb0, kb1) of pair tile `tile`. Whole tiles go round-robin
+// over the pairs for as many full waves as the tile count allows; with `split`, the K-blocks of
+// the remaining tiles (fewer than one per pair) are cut into one contiguous range per pair, so
+// every pair ends at the same point ("stream-K" for the last wave). A range may span the end of
+// one tile and the start of the next: two units. Every unit's accumulator is added into acc by
+// TMA reduce-add, so the pieces of a split tile combine in any order.
+__device__ __forceinline__ bool accum_unit(const AccumParams& p, int pair, int n_pairs, int u,
+                                           int& tile, int& kb0, int& kb1) {
+  const int n_tiles = p.n_pair_rows * p.n_h_tiles, K = p.k_blocks;
+  const int waves = p.split ? n_tiles / n_pairs : (n_tiles + n_pairs - 1) / n_pairs;
+  if (u < waves) {
+    tile = pair + u * n_pairs;
+    kb0 = 0;
+    kb1 = K;
+    return tile < n_tiles;
+  }
+  const int rest = n_tiles - waves * n_pairs;
+  if (!p.split || rest <= 0) return false;
+  // at least kMinSplitBlocks K-blocks per piece, so that the MMAs outweigh the piece's epilogue
+  const long long total = static_cast<long long>(rest) * K;
+  const long long by_size = total / kMinSplitBlocks;
+  const int n_split = by_size < 1 ? 1 : (by_size < n_pairs ? static_cast<int>(by_size) : n_pairs);
+  if (pair >= n_split) return false;
+  const long long g0 = total * pair / n_split, g1 = total * (pair + 1) / n_split;
+  const long long t = g0 / K + (u - waves);
+  const long long b = max(g0, t * K), e = min(g1, (t + 1) * K);
+  if (b >= e) return false;
+  tile = waves * n_pairs + static_cast<int>(t);
+  kb0 = static_cast<int>(b - t * K);
+  kb1 = static_cast<int>(e - t * K);
+  return true;
+}
 
 // Pair tile t covers labelled rows [pr * 256, +256) x hidden columns [ht * 256, +256); the CTA
 // of rank r owns rows pr * 256 + r * 128 + [0, 128) and loads the hidden columns
@@ -511,7 +556,6 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
   pair_setup(ctl, warp, 4);
   const uint32_t tmem_base = ctl->tmem_base;
   volatile int* abort = &ctl->abort;
-  const int n_tiles = p.n_pair_rows * p.n_h_tiles;
   const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
   // A pair tile is rescaled when either of its 128-row blocks moved its reference; both CTAs
   // and every role read the same two flags.
@@ -523,10 +567,11 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
     if (lane == 0) {  // TMA producer (both CTAs)
       int stage = 0, issued = 0;
       uint32_t phase = 0, afull_phase = 0, issued_afull = 0;
-      for (int tile = pair; tile < n_tiles && !*abort; tile += n_pairs) {
+      int tile, kb0, kb1;
+      for (int u = 0; !*abort && accum_unit(p, pair, n_pairs, u, tile, kb0, kb1); ++u) {
         const int ht = tile % p.n_h_tiles, pr = tile / p.n_h_tiles;
         const bool tf = transformed(pr);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort)) break;
           uint8_t* a = smem + stage * STAGE_BYTES;
           const uint32_t lfull = mapa_shared(smem_u32(&ctl->full[stage]), 0);
@@ -561,13 +606,14 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       uint32_t ready_phase = 0;  // bit s: parity of the next phase of ready[s]
-      for (int tile = pair; tile < n_tiles; tile += n_pairs) {
+      int tile, kb0, kb1;
+      for (int u = 0; accum_unit(p, pair, n_pairs, u, tile, kb0, kb1); ++u) {
         if (!mbar_wait(&ctl->tempty[acc], acc_phase ^ 1, abort)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
         const bool tf = transformed(tile / p.n_h_tiles);
         bool ok = true;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           bool landed = mbar_wait(&ctl->full[stage], phase, abort);
           if (landed && tf) {
             landed = mbar_wait(&ctl->ready[stage], (ready_phase >> stage) & 1u, abort);
@@ -583,7 +629,7 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
             // of BK rows x 128 B (LBO = 8 KiB), 16 K-rows = +2 KiB.
             umma_f16_pair(d, smem_desc_sw128(a + k * 32, 16, 1024),
                           smem_desc_sw128(b + k * 2048, 64 * BK * 2, 1024), kIdescAccum,
-                          (kb | k) != 0);
+                          kb != kb0 || k != 0);
           }
           umma_commit_pair(&ctl->empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -599,16 +645,17 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
     const int r_in_tile = (warp - 2 - EPI_WARPS) * 32 + lane;
     int stage = 0;
     uint32_t afull_phase = 0;  // bit s: parity of the next phase of afull[s]
-    for (int tile = pair; tile < n_tiles; tile += n_pairs) {
+    int tile, kb0, kb1;
+    for (int u = 0; accum_unit(p, pair, n_pairs, u, tile, kb0, kb1); ++u) {
       const int pr = tile / p.n_h_tiles;
       if (!transformed(pr)) {  // the MMA consumes these stages untouched
-        stage = (stage + p.k_blocks) % STAGES;
+        stage = (stage + (kb1 - kb0)) % STAGES;
         continue;
       }
       const int row = min(pr * PAIR_ROWS + static_cast<int>(rank) * BM + r_in_tile, p.n_grad - 1);
       const float* sc_row = p.tile_scale + static_cast<long long>(row) * p.n_parts;
       bool ok = true;
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!__all_sync(0xffffffffu, mbar_wait(&ctl->afull[stage], (afull_phase >> stage) & 1u,
                                                 abort))) {
           ok = false;
@@ -649,35 +696,17 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
     uint8_t* buf = staging + g * 16384;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = pair; tile < n_tiles; tile += n_pairs) {
+    int tile, kb0, kb1;
+    for (int u = 0; accum_unit(p, pair, n_pairs, u, tile, kb0, kb1); ++u) {
       const int ht = tile % p.n_h_tiles, pr = tile / p.n_h_tiles;
       // CTA-uniform decision among the 4 epilogue warps (named barriers follow)
       const bool landed = mbar_wait(&ctl->tfull[acc], acc_phase, abort);
       if (named_barrier_or(bar_id, EPI_THREADS, !landed)) break;
       tc_fence_after();
       const int row0 = pr * PAIR_ROWS + static_cast<int>(rank) * BM;
-      const int row = row0 + r_in_tile;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      // acc = alpha * acc + D. Rows that kept their reference have alpha = 1: D is added by
-      // TMA reduce-add (no read of acc at all). A row whose reference moved in this slice has
-      // its acc slice rescaled here first; the first slice stores D.
-      if (!p.first && row < p.n_grad) {
-        const float al = p.alpha[row];
-        if (al != 1.0f) {
-          float4* arow = reinterpret_cast<float4*>(p.acc + static_cast<long long>(row) * p.hidden +
-                                                   ht * BN + g * EPI_COLS);
-          const int n4 = max(0, min(EPI_COLS, p.hidden - ht * BN - g * EPI_COLS)) / 4;
-          for (int v = 0; v < n4; ++v) {
-            float4 o = arow[v];
-            o.x *= al;
-            o.y *= al;
-            o.z *= al;
-            o.w *= al;
-            arow[v] = o;
-          }
-          fence_proxy_async_global();  // the scaled values precede the reduce-adds below
-        }
-      }
+      // acc += D by TMA reduce-add (acc starts at zero; a moved reference was applied to acc
+      // by the combine kernel before this launch)
       const bool any_rows = row0 < p.n_grad;
 #pragma unroll 1
       for (int c = g * (EPI_COLS / 32); c < (g + 1) * (EPI_COLS / 32); ++c) {
@@ -693,11 +722,7 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
           fence_proxy_async_smem();
           named_barrier(bar_id, EPI_THREADS);
           if (elected) {
-            if (p.first) {
-              tma_store_2d(&tm_acc, buf, ht * BN + c * 32, row0);
-            } else {
-              tma_reduce_add_2d(&tm_acc, buf, ht * BN + c * 32, row0);
-            }
+            tma_reduce_add_2d(&tm_acc, buf, ht * BN + c * 32, row0);
             bulk_commit();
           }
         }
@@ -809,9 +834,7 @@ struct Workspace {
   __half* probs[2];      // [n_grad][chunk] each
   float4* partial;       // [n_tokens][chunk / BN]
   float* tile_scale[2];  // [n_grad][chunk / BN] each
-  float* alpha[2];       // [n_grad] each
   int* block_jump;       // [n_slices][flag_stride]
-  int* counters;         // [n_slices][2]: dynamic scheduler counters (logits, accum)
   size_t bytes;
 };
 
@@ -842,14 +865,8 @@ Workspace layout(int64_t n_tokens, int64_t n_grad, int64_t vocab_cols, int64_t v
     w.tile_scale[b] = reinterpret_cast<float*>(base + off);
     if (b < n_buf) off = align_up(off + static_cast<size_t>(n_grad) * tiles * 4, 256);
   }
-  for (int b = 0; b < 2; ++b) {
-    w.alpha[b] = reinterpret_cast<float*>(base + off);
-    if (b < n_buf) off = align_up(off + static_cast<size_t>(n_grad) * 4, 256);
-  }
   w.block_jump = reinterpret_cast<int*>(base + off);
   off = align_up(off + static_cast<size_t>(n_slices) * ((n_grad + BM - 1) / BM + 1) * 4, 256);
-  w.counters = reinterpret_cast<int*>(base + off);
-  off = align_up(off + static_cast<size_t>(n_slices) * 2 * 4, 256);
   w.bytes = off + 256;  // slack for base alignment
   return w;
 }
@@ -1001,9 +1018,11 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
 
   if (cudaMemsetAsync(stats, 0, sizeof(float) * TALM_HEAD_STATS * n_tokens, stream) != cudaSuccess)
     return check_launch("stats memset");
-  // flags and scheduler counters are contiguous in the workspace: one memset for both
-  const size_t zero_bytes = reinterpret_cast<uint8_t*>(ws.counters + n_slices * 2) -
-                            reinterpret_cast<uint8_t*>(ws.block_jump);
+  // every accumulator GEMM adds into acc (TMA reduce-add): it starts at zero
+  if (n_grad > 0 &&
+      cudaMemsetAsync(acc, 0, sizeof(float) * n_grad * hidden_size, stream) != cudaSuccess)
+    return check_launch("acc memset");
+  const size_t zero_bytes = sizeof(int) * n_slices * flag_stride;
   if (cudaMemsetAsync(ws.block_jump, 0, zero_bytes, stream) != cudaSuccess)
     return check_launch("flag memset");
 
@@ -1044,11 +1063,17 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
                               tm_weight, tm_probs, lp, stream, max_pairs);
     }
     if (st != TALM_OK) return st;
+    // the combine rescales acc rows whose reference moved: the previous slice's accumulator
+    // GEMM (on the side stream) must have finished
+    if (pipe && k >= 1 &&
+        cudaStreamWaitEvent(stream, pipe->drained[(k - 1) & 1], 0) != cudaSuccess)
+      return check_launch("wait for the previous accumulator GEMM");
     {
       LaunchTimer timer(TALM_KERNEL_HEAD_COMBINE, stream);
       head_combine_kernel<<<static_cast<int>((n_tokens + 7) / 8), 256, 0, stream>>>(
           ws.partial, n_col_tiles * PARTS, static_cast<int>(n_tokens), static_cast<int>(n_grad), k == 0,
-          stats, ws.tile_scale[buf], ws.alpha[buf], slice_jump);
+          stats, ws.tile_scale[buf], slice_jump, n_grad > 0 ? acc : nullptr,
+          static_cast<int>(hidden_size));
     }
     if ((st = check_launch("head combine kernel")) != TALM_OK) return st;
 
@@ -1066,11 +1091,10 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
       ap.n_parts = n_col_tiles * PARTS;
       ap.n_pair_rows = static_cast<int>((n_grad + PAIR_ROWS - 1) / PAIR_ROWS);
       ap.n_h_tiles = static_cast<int>((hidden_size + BN - 1) / BN);
-      ap.first = k == 0;
+      // a GEMM that runs alone on the caller's stream splits its last wave over all pairs
+      ap.split = pipe ? 0 : 1;
       ap.tile_scale = ws.tile_scale[buf];
-      ap.alpha = ws.alpha[buf];
       ap.block_jump = slice_jump;
-      ap.acc = acc;
       {
         LaunchTimer timer(TALM_KERNEL_HEAD_ACCUM, acc_stream);
         st = launch_pair_kernel(head_accum_kernel, ACCUM_THREADS, ap.n_pair_rows * ap.n_h_tiles, tm_probs,

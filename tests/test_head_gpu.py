@@ -164,6 +164,26 @@ def test_unlabelled_rows_never_produce_nan():
     assert (grad[targets < 0] == 0).all()
 
 
+def test_split_last_wave_matches_reference():
+    """Enough labelled rows (about 5400, 132 accumulator tiles) that the accumulator GEMM fills
+    the GPU on its own and splits its last, partial wave along K over all CTA pairs; planted
+    confident rows move their reference in late slices, so their accumulator rows are rescaled
+    between slices while split pieces of the same tile add into them."""
+    torch.manual_seed(5)
+    n, vocab, size = 6000, 151936, 1536
+    hidden = torch.randn(n, size, device=DEV, dtype=torch.float16) * 2
+    weight = torch.randn(vocab, size, device=DEV) * 0.05
+    targets = torch.randint(0, vocab, (n,), device=DEV)
+    targets[torch.rand(n, device=DEV) < 0.1] = -100
+    cols = [0, 8191, 8192, 65536, 131071, 147455, vocab - 1]
+    planted = _plant(hidden, weight, targets, cols * 40, 40.0)
+    ref = gpu_reference(hidden, weight, targets, grad_scale=3.0)
+    out, grad = _run(hidden, weight, targets, vocab_chunk=8192)
+    check_head(out, ref, grad, "split last wave")
+    assert int(ref["correct"].sum()) >= planted > 0
+    assert torch.equal(out[3], ref["correct"]) or bool(ref["fragile"].any())
+
+
 @pytest.mark.parametrize("n_tokens,vocab,unlabelled",
                          [(700, 151936, 0.45), (37, 151936, 0.3), (300, 1000, 0.0),
                           (300, 1000, 1.0), (5, 4097, 0.5)])
