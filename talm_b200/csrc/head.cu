@@ -12,16 +12,17 @@
 //      labelled rows it writes p = fp16(exp(z - m_t)) into the slice's probability buffer (the
 //      only [rows, chunk] buffer of the head; it stays in L2 at the configured sizes).
 //   2. head_combine_kernel: one warp per row merges the slice's tile statistics with the running
-//      statistics of the earlier slices (log-sum-exp merge), and for labelled rows writes
-//      per-tile factors exp(m_t - m_new); a row whose reference moved has its acc row multiplied
-//      by alpha = exp(m_old - m_new) here (the online-softmax rescale of
-//      solution/fused_head.py:170-177).
-//   3. head_accum_kernel (tcgen05, persistent): acc[256 rows, 256 hidden] += P' W_slice,
-//      K = slice columns, by TMA reduce-add into an acc that starts at zero. P arrives by TMA;
-//      four transform warps rescale it in shared memory to p * exp(m_t - m_new) (so the GEMM
-//      operand equals fp16(exp(z - m_new)), the reference's in-place softmax weights) before the
-//      MMA warp consumes the stage. W_slice is read MN-major (hidden contiguous) straight from
-//      the weight rows. The last, partial wave of tiles is split along K over all CTA pairs.
+//      statistics of the earlier slices (log-sum-exp merge). A row whose reference moved in this
+//      slice (every row on the first slice, afterwards only a row whose max outgrew REF + 8) has
+//      its probability row rescaled in place to p * exp(m_t - m_new), so that it equals
+//      fp16(exp(z - REF_new)), the reference's in-place softmax weights, and its acc row
+//      multiplied by alpha = exp(REF_old - REF_new) (the online-softmax rescale of
+//      solution/fused_head.py:170-177). Every other row's probabilities are already relative to
+//      its reference.
+//   3. head_accum_kernel (tcgen05, persistent): acc[256 rows, 256 hidden] += P W_slice,
+//      K = slice columns, by TMA reduce-add into an acc that starts at zero. P and W_slice go
+//      TMA -> MMA untouched (W read MN-major, hidden contiguous, straight from the weight rows).
+//      The last, partial wave of tiles is split along K over all CTA pairs.
 //
 // A last launch (head_finalize_kernel) turns the statistics into loss / entropy / correctness
 // and the accumulator into dH = acc / s - fp16(W[target]) (fused_head.py:111-125, :160-169),
@@ -59,7 +60,7 @@ constexpr int EPI_WARPS = 4 * EPI_GROUPS;      // 8
 constexpr int EPI_THREADS = 128;               // threads per group
 constexpr int PARTS = EPI_GROUPS;              // statistics records per (row, tile)
 constexpr int LOGITS_THREADS = 32 * (2 + EPI_WARPS);       // producer, MMA, epilogue
-constexpr int ACCUM_THREADS = 32 * (2 + EPI_WARPS + 4);    // + 4 transform warps
+constexpr int ACCUM_THREADS = 32 * (2 + EPI_WARPS);       // producer, MMA, epilogue
 constexpr float kLog2e = 1.4426950408889634f;
 // Slack of the lazy reference: a row's probabilities and accumulator stay relative to REF while
 // its running max is at most REF + kRefSlack, so p = exp(z - REF) <= e^8 (fits fp16).
@@ -78,13 +79,11 @@ __device__ __forceinline__ float ex2(float x) {
 }
 __device__ __forceinline__ float round_f16(float v) { return __half2float(__float2half_rn(v)); }
 
-// Barriers of a CTA of a pair. The pair leader (cluster rank 0) issues every MMA; `full`,
-// `ready` and `tempty` are waited on in the leader only and receive arrivals / transaction
-// bytes from both CTAs; `empty`, `afull` and `tfull` live in each CTA.
+// Barriers of a CTA of a pair. The pair leader (cluster rank 0) issues every MMA; `full` and
+// `tempty` are waited on in the leader only and receive arrivals / transaction bytes from both
+// CTAs; `empty` and `tfull` live in each CTA.
 struct SharedCtl {
   uint64_t full[STAGES];   // leader: both CTAs' operands of the stage landed (TMA bytes)
-  uint64_t afull[STAGES];  // accum kernel, each CTA: its own P half landed (rescaled tiles)
-  uint64_t ready[STAGES];  // accum kernel, leader: both CTAs' transform warps are done
   uint64_t empty[STAGES];  // each CTA: the pair's MMAs finished reading the stage
   uint64_t tfull[2];       // each CTA: its half of an accumulator buffer is complete
   uint64_t tempty[2];      // leader: both CTAs' epilogues drained the buffer
@@ -107,12 +106,10 @@ __device__ __forceinline__ void stage_chunk(uint8_t* buf, int r, int q, uint32_t
 }
 
 // Set-up shared by both GEMMs: barriers, TMEM for the pair, cluster-wide visibility.
-__device__ __forceinline__ void pair_setup(SharedCtl* ctl, int warp, int transform_warps) {
+__device__ __forceinline__ void pair_setup(SharedCtl* ctl, int warp) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&ctl->full[s], 1);
-      mbar_init(&ctl->afull[s], 1);
-      mbar_init(&ctl->ready[s], 2 * transform_warps > 0 ? 2 * transform_warps : 1);
       mbar_init(&ctl->empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -196,7 +193,7 @@ __global__ void __launch_bounds__(LOGITS_THREADS, 1)
     prefetch_tmap(&tm_weight);
     if (p.n_grad > 0) prefetch_tmap(&tm_probs);
   }
-  pair_setup(ctl, warp, 0);
+  pair_setup(ctl, warp);
   const uint32_t tmem_base = ctl->tmem_base;
   volatile int* abort = &ctl->abort;
   const int n_tiles = p.n_pair_rows * p.n_col_tiles;
@@ -407,8 +404,8 @@ __global__ void __launch_bounds__(256) head_combine_kernel(const float4* __restr
                                                            int n_parts, int n_tokens,
                                                            int n_grad, int first,
                                                            float* __restrict__ stats,
-                                                           float* __restrict__ tile_scale,
-                                                           int* __restrict__ block_jump,
+                                                           __half* __restrict__ probs,
+                                                           int probs_ld,
                                                            float* __restrict__ acc, int hidden) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
@@ -442,15 +439,17 @@ __global__ void __launch_bounds__(256) head_combine_kernel(const float4* __restr
   const bool jump = first || m_new > ref + kRefSlack;
   const float ref_new = jump ? m_new : ref;
   // tile sums were taken relative to base_j = (has ref and m_j <= ref + slack) ? ref : m_j
+  // (the factor w_j below is 1 exactly for every part of a row that kept its reference)
+  auto part_factor = [&](const float4& v) {
+    const float base = (!first && v.x <= ref + kRefSlack) ? ref : v.x;
+    return ex2((base - ref_new) * kLog2e);
+  };
   float S = 0.0f, T = 0.0f;
-  float* sc = tile_scale + static_cast<long long>(row) * n_parts;
   for (int j = lane; j < n_parts; j += 32) {
     const float4 v = pr[j];
-    const float base = (!first && v.x <= ref + kRefSlack) ? ref : v.x;
-    const float w = ex2((base - ref_new) * kLog2e);
+    const float w = part_factor(v);
     S = fmaf(v.y, w, S);
     T = fmaf(v.z, w, T);
-    if (row < n_grad) sc[j] = w;  // the accumulator GEMM's factor for this tile (1 if stable)
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -467,11 +466,29 @@ __global__ void __launch_bounds__(256) head_combine_kernel(const float4* __restr
       st[TALM_STAT_BEST] = bv;
       st[TALM_STAT_IDX] = __int_as_float(bi);
     }
-    if (row < n_grad && jump) atomicOr(block_jump + row / BM, 1);
   }
-  // acc = alpha * acc for a row whose reference moved (alpha = 1 for every other row); the
-  // earlier slices' accumulator GEMMs precede this launch, the current slice's follows it
-  if (!first && jump && row < n_grad && acc != nullptr) {
+  if (!jump || row >= n_grad) return;
+  // The row moved its reference: its probabilities of this slice become p * w_j, i.e.
+  // fp16(exp(z - REF_new)) (the stored p was taken relative to base_j), read and written in
+  // 16-byte pieces of 8 columns, EPI_COLS / 8 pieces per part.
+  if (probs != nullptr) {
+    uint4* prow = reinterpret_cast<uint4*>(probs + static_cast<long long>(row) * probs_ld);
+    const int n_pieces = n_parts * (EPI_COLS / 8);
+    for (int c = lane; c < n_pieces; c += 32) {
+      const float w = part_factor(pr[c / (EPI_COLS / 8)]);
+      uint4 q = prow[c];
+      uint32_t* h = reinterpret_cast<uint32_t*>(&q);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<__half2*>(&h[i]));
+        h[i] = pack_half2(f.x * w, f.y * w);
+      }
+      prow[c] = q;
+    }
+  }
+  // acc = alpha * acc (alpha = 1 for every row that kept its reference); the earlier slices'
+  // accumulator GEMMs precede this launch, the current slice's follows it
+  if (!first && acc != nullptr) {
     float4* arow = reinterpret_cast<float4*>(acc + static_cast<long long>(row) * hidden);
     for (int v = lane; v < hidden / 4; v += 32) {
       float4 o = arow[v];
@@ -485,19 +502,16 @@ __global__ void __launch_bounds__(256) head_combine_kernel(const float4* __restr
 }
 
 // ------------------------------------------------------------------------------------------
-// 3. accumulator GEMM: acc += P' W_slice (acc starts at zero; jump rows rescaled by combine)
+// 3. accumulator GEMM: acc += P W_slice (acc starts at zero; moved rows rescaled by combine)
 // ------------------------------------------------------------------------------------------
 struct AccumParams {
   int n_grad;
   int hidden;
   int k_blocks;      // slice columns / BK (padded slice: a multiple of BN / BK)
   int slice_row0;    // first weight row of the slice
-  int n_parts;       // statistics records per row of the slice (the scale table's stride)
   int n_pair_rows;   // ceil(n_grad / PAIR_ROWS)
   int n_h_tiles;     // ceil(hidden / BN)
   int split;         // 1: the tiles of the last, partial wave are split along K over all pairs
-  const float* tile_scale;  // [n_grad][n_parts]: factor per 128 columns
-  const int* block_jump;    // [ceil(n_grad / BM) + 1]: some row of the 128-row block moved its REF
 };
 
 // Work unit u of pair `pair`: K-blocks [kb0, kb1) of pair tile `tile`. Whole tiles go round-robin
@@ -553,40 +567,25 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
     prefetch_tmap(&tm_weight_mn);
     prefetch_tmap(&tm_acc);
   }
-  pair_setup(ctl, warp, 4);
+  pair_setup(ctl, warp);
   const uint32_t tmem_base = ctl->tmem_base;
   volatile int* abort = &ctl->abort;
   const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
-  // A pair tile is rescaled when either of its 128-row blocks moved its reference; both CTAs
-  // and every role read the same two flags.
-  auto transformed = [&](int pr) {
-    return (__ldg(p.block_jump + 2 * pr) | __ldg(p.block_jump + 2 * pr + 1)) != 0;
-  };
 
   if (warp == 0) {
     if (lane == 0) {  // TMA producer (both CTAs)
       int stage = 0, issued = 0;
-      uint32_t phase = 0, afull_phase = 0, issued_afull = 0;
+      uint32_t phase = 0;
       int tile, kb0, kb1;
       for (int u = 0; !*abort && accum_unit(p, pair, n_pairs, u, tile, kb0, kb1); ++u) {
         const int ht = tile % p.n_h_tiles, pr = tile / p.n_h_tiles;
-        const bool tf = transformed(pr);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort)) break;
           uint8_t* a = smem + stage * STAGE_BYTES;
           const uint32_t lfull = mapa_shared(smem_u32(&ctl->full[stage]), 0);
           const int row0 = pr * PAIR_ROWS + rank * BM;
-          if (tf) {
-            // P goes to this CTA's transform warps first; only W is counted on the leader
-            mbar_arrive_expect_tx(&ctl->afull[stage], A_BYTES);
-            tma_load_2d(a, &tm_probs, &ctl->afull[stage], kb * BK, row0);
-            afull_phase ^= 1u << stage;
-            issued_afull |= 1u << stage;
-            if (leader) mbar_arrive_expect_tx(&ctl->full[stage], 2 * B_BYTES);
-          } else {
-            if (leader) mbar_arrive_expect_tx(&ctl->full[stage], 2 * STAGE_BYTES);
-            tma_load_2d_pair(a, &tm_probs, lfull, kb * BK, row0);
-          }
+          if (leader) mbar_arrive_expect_tx(&ctl->full[stage], 2 * STAGE_BYTES);
+          tma_load_2d_pair(a, &tm_probs, lfull, kb * BK, row0);
 #pragma unroll
           for (int j = 0; j < BN / 2 / 64; ++j)
             tma_load_2d_pair(a + A_BYTES + j * (64 * BK * 2), &tm_weight_mn, lfull,
@@ -595,31 +594,20 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
-      // this CTA's own P copies (rescaled tiles) complete on its afull barriers: let the last
-      // one of each stage land before the CTA can leave
-      for (int st = 0; st < STAGES; ++st)
-        if (issued_afull & (1u << st)) mbar_drain(&ctl->afull[st], ((afull_phase >> st) & 1u) ^ 1u);
       if (leader) drain_copies(ctl, stage, phase, issued);
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {  // MMA issuer (leader only)
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
-      uint32_t ready_phase = 0;  // bit s: parity of the next phase of ready[s]
       int tile, kb0, kb1;
       for (int u = 0; accum_unit(p, pair, n_pairs, u, tile, kb0, kb1); ++u) {
         if (!mbar_wait(&ctl->tempty[acc], acc_phase ^ 1, abort)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
-        const bool tf = transformed(tile / p.n_h_tiles);
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb) {
-          bool landed = mbar_wait(&ctl->full[stage], phase, abort);
-          if (landed && tf) {
-            landed = mbar_wait(&ctl->ready[stage], (ready_phase >> stage) & 1u, abort);
-            ready_phase ^= 1u << stage;
-          }
-          if (!landed) { ok = false; break; }
+          if (!mbar_wait(&ctl->full[stage], phase, abort)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a = smem_u32(smem + stage * STAGE_BYTES);
           const uint32_t b = a + A_BYTES;
@@ -640,52 +628,6 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
         if (acc == 0) acc_phase ^= 1;
       }
       drain_mmas(ctl);
-    }
-  } else if (warp >= 2 + EPI_WARPS) {  // transform (both CTAs): p -> p * exp(base - REF_new)
-    const int r_in_tile = (warp - 2 - EPI_WARPS) * 32 + lane;
-    int stage = 0;
-    uint32_t afull_phase = 0;  // bit s: parity of the next phase of afull[s]
-    int tile, kb0, kb1;
-    for (int u = 0; accum_unit(p, pair, n_pairs, u, tile, kb0, kb1); ++u) {
-      const int pr = tile / p.n_h_tiles;
-      if (!transformed(pr)) {  // the MMA consumes these stages untouched
-        stage = (stage + (kb1 - kb0)) % STAGES;
-        continue;
-      }
-      const int row = min(pr * PAIR_ROWS + static_cast<int>(rank) * BM + r_in_tile, p.n_grad - 1);
-      const float* sc_row = p.tile_scale + static_cast<long long>(row) * p.n_parts;
-      bool ok = true;
-      for (int kb = kb0; kb < kb1; ++kb) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&ctl->afull[stage], (afull_phase >> stage) & 1u,
-                                                abort))) {
-          ok = false;
-          break;
-        }
-        afull_phase ^= 1u << stage;
-        const float sc = __ldg(sc_row + (kb * BK) / EPI_COLS);
-        uint4* line = reinterpret_cast<uint4*>(smem + stage * STAGE_BYTES + r_in_tile * 128);
-        // Visit the row's 16-byte chunks in logical order: logical chunk c sits at c ^ (row & 7)
-        // (128-byte swizzle), so the 32 lanes of a warp spread over all 8 chunk positions and
-        // each 512-byte warp access takes the minimum 4 shared-memory wavefronts.
-#pragma unroll
-        for (int c0 = 0; c0 < 8; ++c0) {
-          const int c = c0 ^ (r_in_tile & 7);
-          uint4 v = line[c];
-          uint32_t* w = reinterpret_cast<uint32_t*>(&v);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            __half2 h = *reinterpret_cast<__half2*>(&w[i]);
-            const float2 f = __half22float2(h);
-            w[i] = pack_half2(f.x * sc, f.y * sc);
-          }
-          line[c] = v;
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&ctl->ready[stage]), 0));
-        if (++stage == STAGES) stage = 0;
-      }
-      if (!ok) break;
     }
   } else {  // epilogue: warps 2..9 of both CTAs
     const int q = warp & 3;
@@ -832,9 +774,7 @@ __global__ void __launch_bounds__(256) head_merge_shards_kernel(const float* __r
 // while the logits GEMM and the combine of slice k + 1 (caller's stream) write the other one.
 struct Workspace {
   __half* probs[2];      // [n_grad][chunk] each
-  float4* partial;       // [n_tokens][chunk / BN]
-  float* tile_scale[2];  // [n_grad][chunk / BN] each
-  int* block_jump;       // [n_slices][flag_stride]
+  float4* partial;       // [n_tokens][chunk / EPI_COLS]
   size_t bytes;
 };
 
@@ -861,12 +801,6 @@ Workspace layout(int64_t n_tokens, int64_t n_grad, int64_t vocab_cols, int64_t v
   }
   w.partial = reinterpret_cast<float4*>(base + off);
   off = align_up(off + static_cast<size_t>(n_tokens) * tiles * 16, 256);
-  for (int b = 0; b < 2; ++b) {
-    w.tile_scale[b] = reinterpret_cast<float*>(base + off);
-    if (b < n_buf) off = align_up(off + static_cast<size_t>(n_grad) * tiles * 4, 256);
-  }
-  w.block_jump = reinterpret_cast<int*>(base + off);
-  off = align_up(off + static_cast<size_t>(n_slices) * ((n_grad + BM - 1) / BM + 1) * 4, 256);
   w.bytes = off + 256;  // slack for base alignment
   return w;
 }
@@ -1005,7 +939,6 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
   if (st != TALM_OK) return st;
 
   const int64_t n_slices = (vocab_cols + chunk - 1) / chunk;
-  const int64_t flag_stride = (n_grad + BM - 1) / BM + 1;
   std::lock_guard<std::mutex> lock(g_pipe_mutex);
   // The accumulator GEMM goes to the side stream (overlapping the next slice's logits GEMM)
   // only when it has fewer tiles than the GPU has SMs; a GEMM that fills the GPU on its own
@@ -1022,9 +955,6 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
   if (n_grad > 0 &&
       cudaMemsetAsync(acc, 0, sizeof(float) * n_grad * hidden_size, stream) != cudaSuccess)
     return check_launch("acc memset");
-  const size_t zero_bytes = sizeof(int) * n_slices * flag_stride;
-  if (cudaMemsetAsync(ws.block_jump, 0, zero_bytes, stream) != cudaSuccess)
-    return check_launch("flag memset");
 
   const int k_blocks = static_cast<int>((hidden_size + BK - 1) / BK);
   const int n_pair_rows = static_cast<int>((n_tokens + PAIR_ROWS - 1) / PAIR_ROWS);
@@ -1034,7 +964,6 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
     const int buf = static_cast<int>(k & 1);
     const int cols = static_cast<int>(vocab_cols - s0 < chunk ? vocab_cols - s0 : chunk);
     const int n_col_tiles = (cols + BN - 1) / BN;
-    int* slice_jump = ws.block_jump + k * flag_stride;
     // the pair of buffers this slice writes is free once slice k - 2's accumulator GEMM is done
     if (pipe && k >= 2 && cudaStreamWaitEvent(stream, pipe->drained[buf], 0) != cudaSuccess)
       return check_launch("wait for slice buffers");
@@ -1064,7 +993,8 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
     }
     if (st != TALM_OK) return st;
     // the combine rescales acc rows whose reference moved: the previous slice's accumulator
-    // GEMM (on the side stream) must have finished
+    // GEMM (on the side stream) must have finished. (The probability rows it rescales are this
+    // slice's, in the buffer the logits GEMM just wrote.)
     if (pipe && k >= 1 &&
         cudaStreamWaitEvent(stream, pipe->drained[(k - 1) & 1], 0) != cudaSuccess)
       return check_launch("wait for the previous accumulator GEMM");
@@ -1072,8 +1002,8 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
       LaunchTimer timer(TALM_KERNEL_HEAD_COMBINE, stream);
       head_combine_kernel<<<static_cast<int>((n_tokens + 7) / 8), 256, 0, stream>>>(
           ws.partial, n_col_tiles * PARTS, static_cast<int>(n_tokens), static_cast<int>(n_grad), k == 0,
-          stats, ws.tile_scale[buf], slice_jump, n_grad > 0 ? acc : nullptr,
-          static_cast<int>(hidden_size));
+          stats, n_grad > 0 ? ws.probs[buf] : nullptr, static_cast<int>(chunk),
+          n_grad > 0 ? acc : nullptr, static_cast<int>(hidden_size));
     }
     if ((st = check_launch("head combine kernel")) != TALM_OK) return st;
 
@@ -1088,13 +1018,10 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
       ap.hidden = static_cast<int>(hidden_size);
       ap.k_blocks = n_col_tiles * (BN / BK);
       ap.slice_row0 = static_cast<int>(s0);
-      ap.n_parts = n_col_tiles * PARTS;
       ap.n_pair_rows = static_cast<int>((n_grad + PAIR_ROWS - 1) / PAIR_ROWS);
       ap.n_h_tiles = static_cast<int>((hidden_size + BN - 1) / BN);
       // a GEMM that runs alone on the caller's stream splits its last wave over all pairs
       ap.split = pipe ? 0 : 1;
-      ap.tile_scale = ws.tile_scale[buf];
-      ap.block_jump = slice_jump;
       {
         LaunchTimer timer(TALM_KERNEL_HEAD_ACCUM, acc_stream);
         st = launch_pair_kernel(head_accum_kernel, ACCUM_THREADS, ap.n_pair_rows * ap.n_h_tiles, tm_probs,
