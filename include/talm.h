@@ -58,9 +58,10 @@ int talm_device_status(int* status_out);
 #define TALM_KERNEL_HEAD_ACCUM 2    /* head_accum_kernel    (tcgen05 accumulator GEMM)    */
 #define TALM_KERNEL_HEAD_FINALIZE 3 /* head_finalize_kernel                               */
 #define TALM_KERNEL_HEAD_MERGE 4    /* head_merge_shards_kernel                           */
-#define TALM_KERNEL_NF4 5           /* nf4 chunk kernel (16-byte vectorised main body)    */
+#define TALM_KERNEL_NF4 5           /* nf4 bulk-copy and chunk kernels (main body)        */
 #define TALM_KERNEL_NF4_TAIL 6      /* nf4 byte kernel (tails, unaligned pointers)        */
-#define TALM_KERNEL_KINDS 7
+#define TALM_KERNEL_HEAD_SCALE 7    /* head_scale_grad_kernel (backward scaling)          */
+#define TALM_KERNEL_KINDS 8
 int talm_profile_begin(void);
 int talm_profile_end(double* ms_out, int64_t* launches_out, int n_kinds);
 
@@ -188,6 +189,20 @@ int talm_head_finalize(const float* stats, const int64_t* targets, int64_t n_tok
  * vocabulary-parallel head (log-sum-exp merge of online-softmax partials). */
 int talm_head_combine(const float* gathered, int64_t n_shards, int64_t n_tokens, int64_t rank,
                       int64_t n_grad, float* stats_out, float* acc_scale, void* stream);
+
+/* The head's backward: out = out_dtype(float(fp16(grad)) * s), s = grad_loss / denom, or 0
+ * when denom == 0 (grad_loss, denom: fp32 scalars in device memory). grad is [n_rows, n_cols]
+ * with a row stride of ld_grad elements, fp16 (grad_is_f32 == 0) or fp32 (grad_is_f32 != 0:
+ * rounded to fp16 first, the value the single-GPU forward saves); out is a contiguous
+ * [n_rows, n_cols] array of out_dtype (TALM_DTYPE_*).
+ * Replaces _head_backward (fused_head.py:280-287): the reference's chain of four elementwise
+ * torch passes (to fp32, scale, where, to the hidden's dtype) in one. */
+#define TALM_DTYPE_F16 0
+#define TALM_DTYPE_BF16 1
+#define TALM_DTYPE_F32 2
+int talm_head_scale_grad(const void* grad, int64_t ld_grad, int grad_is_f32,
+                         const float* grad_loss, const float* denom, int64_t n_rows,
+                         int64_t n_cols, void* out, int out_dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -139,6 +139,14 @@ def head_reference64(hidden, weight, targets, num_items=None):
     }
 
 
+def scale_grad(grad_hidden, grad_loss, denom, out_dtype):
+    """The head's backward (solution/fused_head.py:280-287): the saved fp16 hidden gradient
+    times grad_loss / denom in fp32, 0 where denom == 0, in the hidden's dtype."""
+    scale = grad_loss.to(torch.float32) / denom
+    scale = torch.where(denom != 0, scale, 0.0)
+    return (grad_hidden.to(F16).to(torch.float32) * scale).to(out_dtype)
+
+
 class CpuHeadOps:
     """The three kernel steps of talm_b200.vocab_parallel (shard / combine / finalize) restated
     on CPU tensors, so that the exchange logic runs on gloo ranks in the tests."""

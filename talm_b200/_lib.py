@@ -36,6 +36,7 @@ SIGNATURES = {
     "talm_head_finalize": (_INT, [_P, _P, _I64, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _P,
                                   _P, _P, _P, _P, _INT, _P]),
     "talm_head_combine": (_INT, [_P, _I64, _I64, _I64, _I64, _P, _P, _P]),
+    "talm_head_scale_grad": (_INT, [_P, _I64, _INT, _P, _P, _I64, _I64, _P, _INT, _P]),
 }
 
 # Mirrors include/talm.h.
@@ -86,7 +87,7 @@ def stream_of(device):
 
 
 KERNEL_KINDS = ("head_logits", "head_combine", "head_accum", "head_finalize", "head_merge",
-                "nf4", "nf4_tail")
+                "nf4", "nf4_tail", "head_scale")
 
 
 def profile_begin():

@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cuda.h>  // CUtensorMap (type only; the driver entry point is fetched at run time)
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>

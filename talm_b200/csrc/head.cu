@@ -689,7 +689,7 @@ __global__ void __launch_bounds__(256) head_finalize_kernel(
     const __half* __restrict__ weight, long long ld_weight, long long col0, long long vcols,
     int hidden, const long long* __restrict__ grad_rows, float* __restrict__ token_loss,
     float* __restrict__ token_entropy, int* __restrict__ correct, void* __restrict__ grad,
-    int grad_f32) {
+    int grad_f32, int vec4) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
   if (row >= n_tokens) return;
@@ -713,18 +713,98 @@ __global__ void __launch_bounds__(256) head_finalize_kernel(
   const float* arow = acc + static_cast<long long>(row) * hidden;
   const __half* wrow = weight + (own ? (tgt - col0) * ld_weight : 0);
   const float scale = acc_scale ? acc_scale[row] : 0.0f;
-  for (int h = lane; h < hidden; h += 32) {
-    float g = 0.0f;
-    if (live) {
-      const float a = arow[h];
-      g = acc_scale ? a * scale : a / s;
-      if (own) g -= __half2float(wrow[h]);
+  auto value = [&](float a, __half w) {
+    if (!live) return 0.0f;
+    const float g = acc_scale ? a * scale : a / s;
+    return own ? g - __half2float(w) : g;
+  };
+  if (vec4) {  // 4 columns per lane and step: 16-byte acc loads, 8- or 16-byte stores
+    const __half zero = __float2half_rn(0.0f);
+    for (int h = 4 * lane; h < hidden; h += 128) {
+      const float4 a = live ? *reinterpret_cast<const float4*>(arow + h) : make_float4(0, 0, 0, 0);
+      __half2 w01 = __halves2half2(zero, zero), w23 = w01;
+      if (own) {
+        const uint2 wv = *reinterpret_cast<const uint2*>(wrow + h);
+        w01 = *reinterpret_cast<const __half2*>(&wv.x);
+        w23 = *reinterpret_cast<const __half2*>(&wv.y);
+      }
+      const float g0 = value(a.x, __low2half(w01)), g1 = value(a.y, __high2half(w01));
+      const float g2 = value(a.z, __low2half(w23)), g3 = value(a.w, __high2half(w23));
+      if (grad_f32) {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(grad) + out * hidden + h) =
+            make_float4(g0, g1, g2, g3);
+      } else {
+        *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(grad) + out * hidden + h) =
+            make_uint2(pack_half2(g0, g1), pack_half2(g2, g3));
+      }
     }
+    return;
+  }
+  for (int h = lane; h < hidden; h += 32) {
+    const float g = value(live ? arow[h] : 0.0f, own ? wrow[h] : __float2half_rn(0.0f));
     if (grad_f32) {
       reinterpret_cast<float*>(grad)[out * hidden + h] = g;
     } else {
       reinterpret_cast<__half*>(grad)[out * hidden + h] = __float2half_rn(g);
     }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// 5. backward: the saved gradient times grad_loss / denom, in the hidden's dtype
+// ------------------------------------------------------------------------------------------
+template <int OUT>
+__device__ __forceinline__ void store_scaled(void* out, long long i, float v) {
+  if (OUT == TALM_DTYPE_F16) {
+    reinterpret_cast<__half*>(out)[i] = __float2half_rn(v);
+  } else if (OUT == TALM_DTYPE_BF16) {
+    reinterpret_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+  } else {
+    reinterpret_cast<float*>(out)[i] = v;
+  }
+}
+
+// One thread per 4 consecutive columns of a row (the row length is a multiple of 4 on the
+// vector path, checked by the host); any other shape goes one element per thread.
+template <int OUT, bool IN_F32, bool VEC4>
+__global__ void __launch_bounds__(256) head_scale_grad_kernel(
+    const void* __restrict__ grad, long long ld, const float* __restrict__ grad_loss,
+    const float* __restrict__ denom, long long n_rows, long long n_cols, void* __restrict__ out) {
+  const float d = *denom;
+  // fused_head.py:280-287: (grad_loss / denom, then 0 where denom == 0) in fp32
+  const float sc = d != 0.0f ? *grad_loss / d : 0.0f;
+  const long long per_row = VEC4 ? n_cols / 4 : n_cols;
+  const long long n = n_rows * per_row;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += stride) {
+    const long long r = i / per_row, c = (i - r * per_row) * (VEC4 ? 4 : 1);
+    float v[4];
+    constexpr int W = VEC4 ? 4 : 1;
+    if (IN_F32) {
+      const float* src = reinterpret_cast<const float*>(grad) + r * ld + c;
+      if (VEC4) {
+        const float4 q = *reinterpret_cast<const float4*>(src);
+        v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+      } else {
+        v[0] = *src;
+      }
+#pragma unroll
+      for (int k = 0; k < W; ++k) v[k] = __half2float(__float2half_rn(v[k]));
+    } else {
+      const __half* src = reinterpret_cast<const __half*>(grad) + r * ld + c;
+      if (VEC4) {
+        const uint2 q = *reinterpret_cast<const uint2*>(src);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&q.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&q.y));
+        v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+      } else {
+        v[0] = __half2float(*src);
+      }
+    }
+    const long long o = r * n_cols + c;
+#pragma unroll
+    for (int k = 0; k < W; ++k) store_scaled<OUT>(out, o + k, v[k] * sc);
   }
 }
 
@@ -1051,6 +1131,10 @@ int talm_head_finalize(const float* stats, const int64_t* targets, int64_t n_tok
   if (!stats || !targets) return set_error(TALM_EINVAL, "null pointer");
   if (grad != nullptr && n_grad > 0 && (acc == nullptr || weight == nullptr))
     return set_error(TALM_EINVAL, "gradient needs acc and weight");
+  // 4 columns per lane when every row of acc, grad and weight starts on the needed boundary
+  auto aligned = [](const void* q, uintptr_t a) { return (reinterpret_cast<uintptr_t>(q) & (a - 1)) == 0; };
+  const int vec4 = hidden_size % 4 == 0 && ld_weight % 4 == 0 && aligned(acc, 16) &&
+                   aligned(weight, 8) && aligned(grad, grad_is_f32 ? 16 : 8);
   LaunchTimer timer(TALM_KERNEL_HEAD_FINALIZE, static_cast<cudaStream_t>(stream));
   head::head_finalize_kernel<<<static_cast<int>((n_tokens + 7) / 8), 256, 0,
                                static_cast<cudaStream_t>(stream)>>>(
@@ -1058,8 +1142,52 @@ int talm_head_finalize(const float* stats, const int64_t* targets, int64_t n_tok
       static_cast<int>(n_grad), acc, acc_scale, reinterpret_cast<const __half*>(weight),
       ld_weight, vocab_col0, vocab_cols, static_cast<int>(hidden_size),
       reinterpret_cast<const long long*>(grad_rows), token_loss, token_entropy, correct, grad,
-      grad_is_f32);
+      grad_is_f32, vec4);
   return check_launch("head finalize kernel");
+}
+
+int talm_head_scale_grad(const void* grad, int64_t ld_grad, int grad_is_f32,
+                         const float* grad_loss, const float* denom, int64_t n_rows,
+                         int64_t n_cols, void* out, int out_dtype, void* stream) {
+  using namespace talm;
+  if (n_rows < 0 || n_cols < 0 || ld_grad < n_cols)
+    return set_error(TALM_EINVAL, "need n_rows, n_cols >= 0 and ld_grad >= n_cols");
+  if (out_dtype < TALM_DTYPE_F16 || out_dtype > TALM_DTYPE_F32)
+    return set_error(TALM_EINVAL, "out_dtype must be TALM_DTYPE_F16, _BF16 or _F32");
+  if (n_rows == 0 || n_cols == 0) return TALM_OK;
+  if (!grad || !grad_loss || !denom || !out) return set_error(TALM_EINVAL, "null pointer");
+  const int in_bytes = grad_is_f32 ? 4 : 2, out_bytes = out_dtype == TALM_DTYPE_F32 ? 4 : 2;
+  auto aligned = [](const void* q, uintptr_t a) { return (reinterpret_cast<uintptr_t>(q) & (a - 1)) == 0; };
+  const bool vec4 = n_cols % 4 == 0 && ld_grad % 4 == 0 && aligned(grad, 4 * in_bytes) &&
+                    aligned(out, 4 * out_bytes);
+  const long long items = n_rows * (vec4 ? n_cols / 4 : n_cols);
+  const int sms = current_sm_count();
+  if (sms <= 0) return set_error(TALM_ENODEV, "no CUDA device");
+  const long long want = (items + 255) / 256;
+  const int grid = static_cast<int>(want < int64_t{sms} * 8 ? want : int64_t{sms} * 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LaunchTimer timer(TALM_KERNEL_HEAD_SCALE, s);
+#define TALM_SCALE_LAUNCH(OUT, F32, V)                                                        \
+  head::head_scale_grad_kernel<OUT, F32, V><<<grid, 256, 0, s>>>(grad, ld_grad, grad_loss, \
+                                                                 denom, n_rows, n_cols, out)
+#define TALM_SCALE_BY_INPUT(OUT)                                          \
+  do {                                                                    \
+    if (grad_is_f32) {                                                    \
+      if (vec4) TALM_SCALE_LAUNCH(OUT, true, true); else TALM_SCALE_LAUNCH(OUT, true, false);   \
+    } else {                                                              \
+      if (vec4) TALM_SCALE_LAUNCH(OUT, false, true); else TALM_SCALE_LAUNCH(OUT, false, false); \
+    }                                                                     \
+  } while (0)
+  if (out_dtype == TALM_DTYPE_F16) {
+    TALM_SCALE_BY_INPUT(TALM_DTYPE_F16);
+  } else if (out_dtype == TALM_DTYPE_BF16) {
+    TALM_SCALE_BY_INPUT(TALM_DTYPE_BF16);
+  } else {
+    TALM_SCALE_BY_INPUT(TALM_DTYPE_F32);
+  }
+#undef TALM_SCALE_BY_INPUT
+#undef TALM_SCALE_LAUNCH
+  return check_launch("head scale kernel");
 }
 
 int talm_head_combine(const float* gathered, int64_t n_shards, int64_t n_tokens, int64_t rank,

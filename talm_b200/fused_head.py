@@ -44,12 +44,29 @@ def _denominator(num_items, labelled_count):
     return torch.tensor(float(num_items), device=labelled_count.device)
 
 
+_OUT_DTYPES = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}  # TALM_DTYPE_*
+
+
 def _head_backward(ctx, grad_loss):
-    """dH * grad_loss / denom, 0 when denom == 0, in the hidden's dtype (fused_head.py:280-287)."""
+    """dH * grad_loss / denom, 0 when denom == 0, in the hidden's dtype (fused_head.py:280-287),
+    in one kernel (talm_head_scale_grad). The saved gradient is fp16, or the fp32 all-reduced
+    one of the vocabulary-parallel head (rounded to fp16 inside the kernel first)."""
     (grad_hidden,) = ctx.saved_tensors
-    scale = grad_loss.to(torch.float32) / ctx.denom
-    scale = torch.where(ctx.denom != 0, scale, 0.0)
-    return (grad_hidden.to(torch.float32) * scale).to(ctx.out_dtype)
+    if ctx.out_dtype not in _OUT_DTYPES:
+        raise TypeError(f"hidden dtype {ctx.out_dtype} not supported by the head's backward")
+    lib = _lib.load()
+    device = grad_hidden.device
+    n_rows, n_cols = grad_hidden.shape
+    out = torch.empty(n_rows, n_cols, dtype=ctx.out_dtype, device=device)
+    if grad_hidden.stride(1) != 1:
+        grad_hidden = grad_hidden.contiguous()
+    gl = grad_loss.detach().to(device=device, dtype=torch.float32).reshape(())
+    denom = ctx.denom.detach().to(device=device, dtype=torch.float32).reshape(())
+    _lib.check(lib.talm_head_scale_grad(
+        _lib.ptr(grad_hidden), grad_hidden.stride(0), int(grad_hidden.dtype == torch.float32),
+        _lib.ptr(gl), _lib.ptr(denom), n_rows, n_cols, _lib.ptr(out), _OUT_DTYPES[ctx.out_dtype],
+        _lib.stream_of(device)), "talm_head_scale_grad")
+    return out
 
 
 def labelled_first(labelled, n_labelled):

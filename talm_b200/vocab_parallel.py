@@ -89,8 +89,9 @@ OPS = CudaHeadOps()
 def sharded_head(hidden, weight_shard, targets, vocab, col0, num_items=None, vocab_chunk=8192,
                  need_grad=True, n_labelled=None, group=None, ops=None):
     """One rank's part of the vocabulary-parallel head. Returns (loss, token_loss, entropy,
-    correct, grad_hidden) with grad_hidden the all-reduced dH (unscaled by the loss
-    denominator, in the hidden's dtype) or None; every rank gets the same values."""
+    correct, grad_hidden) with grad_hidden the all-reduced dH in fp32 (unscaled by the loss
+    denominator; the backward rounds it to fp16, the value the single-GPU head saves) or None;
+    every rank gets the same values."""
     ops = ops or OPS
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
@@ -120,7 +121,7 @@ def sharded_head(hidden, weight_shard, targets, vocab, col0, num_items=None, voc
         merged, rows_targets, n_grad, acc, scale, w16, ld_w, col0, cols, src, need_grad)
     if grad is not None:
         dist.all_reduce(grad, group=group)
-        grad = grad[:, :hidden_size].to(torch.float16)
+        grad = grad[:, :hidden_size]
     denom = _denominator(num_items, labelled.sum())
     loss = token_loss.sum() / denom
     return loss, token_loss, token_entropy, correct.to(torch.bool), grad

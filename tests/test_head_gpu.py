@@ -262,3 +262,29 @@ def test_device_status_clean_after_runs():
     from talm_b200 import _lib
 
     assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_backward_scale_kernel_matches_oracle(out_dtype):
+    """talm_head_scale_grad against the reference's backward expression (fused_head.py:280-287):
+    fp16 and fp32 saved gradients, a padded row stride, an odd row length, denom 0 - bit-exact."""
+    from types import SimpleNamespace
+
+    from oracle.head import scale_grad
+    from talm_b200.fused_head import _head_backward
+
+    torch.manual_seed(11)
+    cases = [torch.randn(37, 40, device=DEV).half(),
+             torch.randn(37, 48, device=DEV).half()[:, :40],
+             torch.randn(1000, 1536, device=DEV) * 3,
+             torch.randn(5, 13, device=DEV).half(),
+             torch.randn(6, 13, device=DEV)]
+    for g in cases:
+        for gl, dn in ((2.5, 7.0), (1.0, 3.0), (4.0, 0.0)):
+            gl_t = torch.tensor(gl, device=DEV)
+            ctx = SimpleNamespace(saved_tensors=(g,), denom=torch.tensor(dn, device=DEV),
+                                  out_dtype=out_dtype)
+            out = _head_backward(ctx, gl_t)
+            ref = scale_grad(g, gl_t, ctx.denom, out_dtype)
+            assert out.dtype == out_dtype and out.shape == g.shape
+            assert torch.equal(out, ref), (tuple(g.shape), g.dtype, gl, dn)

@@ -120,12 +120,17 @@ def test_denominator_and_backward_scale():
     assert float(fused_head._denominator(None, count)) == 1.0
     assert float(fused_head._denominator(7, count)) == 7.0
     assert float(fused_head._denominator(torch.tensor(5), count)) == 5.0
-    ctx = SimpleNamespace(saved_tensors=(torch.ones(2, 3, dtype=torch.float16),),
-                          denom=torch.tensor(0.0), out_dtype=torch.float32)
-    out = fused_head._head_backward(ctx, torch.tensor(2.0))
+    # the backward's semantics (the oracle restatement the GPU kernel is checked against)
+    from oracle.head import scale_grad
+
+    ones = torch.ones(2, 3, dtype=torch.float16)
+    out = scale_grad(ones, torch.tensor(2.0), torch.tensor(0.0), torch.float32)
     assert out.dtype == torch.float32 and torch.equal(out, torch.zeros(2, 3))
-    ctx.denom = torch.tensor(4.0)
-    assert torch.equal(fused_head._head_backward(ctx, torch.tensor(2.0)), torch.full((2, 3), .5))
+    assert torch.equal(scale_grad(ones, torch.tensor(2.0), torch.tensor(4.0), torch.float32),
+                       torch.full((2, 3), .5))
+    # an fp32 gradient is rounded to fp16 first
+    g = torch.tensor([[1.0 + 2 ** -13]])
+    assert float(scale_grad(g, torch.tensor(1.0), torch.tensor(1.0), torch.float32)) == 1.0
 
 
 def test_labelled_first_is_order_stable():
