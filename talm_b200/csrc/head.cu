@@ -30,6 +30,7 @@
 #include <math.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -45,9 +46,11 @@ constexpr int A_BYTES = BM * BK * 2;        // 16 KiB: this CTA's 128 rows of A
 constexpr int B_BYTES = (BN / 2) * BK * 2;  // 16 KiB: this CTA's half of B's columns
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;           // double-buffered fp32 accumulator (128 x 256 per CTA)
-// Epilogue staging: two 16 KiB buffers (128 rows x 128 bytes, 128-byte swizzle) through which
-// the epilogue's outputs leave by TMA store / reduce-add instead of per-lane global stores.
-constexpr int STAGING_BYTES = 2 * 16384;
+// Epilogue staging: four 16 KiB buffers (128 rows x 128 bytes, 128-byte swizzle), two per
+// epilogue group used in turn, through which the epilogue's outputs leave by TMA store /
+// reduce-add instead of per-lane global stores; a group fills one buffer while the store of
+// the other is still reading it.
+constexpr int STAGING_BYTES = 4 * 16384;
 constexpr int SMEM_BYTES =
     STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align slack*/ + 512 /*barriers*/;
 // Two epilogue groups of 4 warps (one warp per TMEM lane quarter in each group); group g owns
@@ -254,7 +257,8 @@ __global__ void __launch_bounds__(LOGITS_THREADS, 1)
     const int bar_id = 1 + g;
     const int r_in_tile = q * 32 + lane;
     const bool elected = (warp - 2) % 4 == 0 && lane == 0;  // the group's TMA-issuing thread
-    uint8_t* buf = staging + g * 16384;
+    uint8_t* const bufs = staging + g * 2 * 16384;  // the group's two staging buffers
+    int nb = 0;                                     // the one to fill next
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = pair; tile < n_tiles; tile += n_pairs) {
@@ -294,8 +298,11 @@ __global__ void __launch_bounds__(LOGITS_THREADS, 1)
       uint32_t r[32];
       // One 32-column chunk: `track` = max / argmax / target, `sum` = s, t and the
       // probabilities (written to `buf`, 16-byte chunks qbase..qbase+3 of this row). The TMEM
-      // load is warp-collective (.sync.aligned): every lane executes it.
-      auto chunk = [&](int c, bool track, bool sum, float mscaled, uint8_t* buf, int qbase) {
+      // load is warp-collective (.sync.aligned): every lane executes it. `full` (a compile-time
+      // flag: the group's columns are all valid) drops the per-column bounds tests.
+      auto chunk = [&](auto full, int c, bool track, bool sum, float mscaled, uint8_t* buf,
+                       int qbase) {
+        constexpr bool kFull = decltype(full)::value;
         tmem_ld_32x32b_x32(taddr + c * 32, r);
         tmem_wait_ld();
         uint32_t packed[16];
@@ -305,8 +312,8 @@ __global__ void __launch_bounds__(LOGITS_THREADS, 1)
           // fp16 rounding of the pair as the reference's fp16 GEMM output (one packed cvt)
           const float2 z = __half22float2(
               __floats2half2_rn(__uint_as_float(r[j]), __uint_as_float(r[j + 1])));
-          const bool ok0 = full_tile || col < ncols;
-          const bool ok1 = full_tile || col + 1 < ncols;
+          const bool ok0 = kFull || col < ncols;
+          const bool ok1 = kFull || col + 1 < ncols;
           if (track) {
             if (ok0 && z.x > mx) { mx = z.x; arg = col; }
             if (ok1 && z.y > mx) { mx = z.y; arg = col + 1; }
@@ -333,16 +340,20 @@ __global__ void __launch_bounds__(LOGITS_THREADS, 1)
       };
       // A pass with sums over the group's columns: 2 blocks of 64 columns, each staged and
       // stored. `base` per lane; `track` for the single-pass case.
-      auto sum_pass = [&](bool track, float base) {
+      auto sum_pass = [&](auto full, bool track, float base) {
         const float mscaled = base * kLog2e;
 #pragma unroll 1
         for (int kb = g * (EPI_COLS / 64); kb < (g + 1) * (EPI_COLS / 64); ++kb) {
+          uint8_t* buf = bufs + nb * 16384;
           if (store_p) {
-            if (elected) bulk_wait_read<0>();  // the group's previous store has read `buf`
+            // the store issued from this buffer two blocks ago has read it (at most the last
+            // store, from the other buffer, may still be reading)
+            if (elected) bulk_wait_read<1>();
             named_barrier(bar_id, EPI_THREADS);
+            nb ^= 1;
           }
-          chunk(2 * kb, track, true, mscaled, store_p ? buf : nullptr, 0);
-          chunk(2 * kb + 1, track, true, mscaled, store_p ? buf : nullptr, 4);
+          chunk(full, 2 * kb, track, true, mscaled, store_p ? buf : nullptr, 0);
+          chunk(full, 2 * kb + 1, track, true, mscaled, store_p ? buf : nullptr, 4);
           if (store_p) {
             fence_proxy_async_smem();
             named_barrier(bar_id, EPI_THREADS);
@@ -353,25 +364,33 @@ __global__ void __launch_bounds__(LOGITS_THREADS, 1)
           }
         }
       };
-      if (p.has_ref) {
-        s = 0.0f;
-        t = 0.0f;
-        sum_pass(true, ref);
-        const bool jump = mx > ref + kRefSlack;
-        if (named_barrier_or(bar_id, EPI_THREADS, jump)) {
-          // some row's reference moves in the group's columns: they are redone (rows without
-          // a move recompute the same values); earlier stores must land before the new ones
-          if (elected) bulk_wait_all();
-          named_barrier(bar_id, EPI_THREADS);
+      auto epilogue = [&](auto full) {
+        if (p.has_ref) {
           s = 0.0f;
           t = 0.0f;
-          sum_pass(false, jump ? mx : ref);
-        }
-      } else {
+          sum_pass(full, true, ref);
+          const bool jump = mx > ref + kRefSlack;
+          if (named_barrier_or(bar_id, EPI_THREADS, jump)) {
+            // some row's reference moves in the group's columns: they are redone (rows
+            // without a move recompute the same values); earlier stores must land before the
+            // new ones
+            if (elected) bulk_wait_all();
+            named_barrier(bar_id, EPI_THREADS);
+            s = 0.0f;
+            t = 0.0f;
+            sum_pass(full, false, jump ? mx : ref);
+          }
+        } else {
 #pragma unroll 1
-        for (int c = g * (EPI_COLS / 32); c < (g + 1) * (EPI_COLS / 32); ++c)
-          chunk(c, true, false, 0.0f, nullptr, 0);
-        sum_pass(false, mx);
+          for (int c = g * (EPI_COLS / 32); c < (g + 1) * (EPI_COLS / 32); ++c)
+            chunk(full, c, true, false, 0.0f, nullptr, 0);
+          sum_pass(full, false, mx);
+        }
+      };
+      if (full_tile) {
+        epilogue(std::true_type{});
+      } else {
+        epilogue(std::false_type{});
       }
       tc_fence_before();
       __syncwarp();
@@ -635,7 +654,8 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
     const int bar_id = 1 + g;
     const int r_in_tile = q * 32 + lane;
     const bool elected = (warp - 2) % 4 == 0 && lane == 0;  // the group's TMA-issuing thread
-    uint8_t* buf = staging + g * 16384;
+    uint8_t* const bufs = staging + g * 2 * 16384;  // the group's two staging buffers
+    int nb = 0;                                     // the one to fill next
     int acc = 0;
     uint32_t acc_phase = 0;
     int tile, kb0, kb1;
@@ -656,7 +676,10 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
         tmem_ld_32x32b_x32(taddr + c * 32, r);
         tmem_wait_ld();
         if (any_rows && ht * BN + c * 32 < p.hidden) {
-          if (elected) bulk_wait_read<0>();  // the group's previous reduce has read `buf`
+          uint8_t* buf = bufs + nb * 16384;
+          nb ^= 1;
+          // the reduce issued from this buffer two chunks ago has read it
+          if (elected) bulk_wait_read<1>();
           named_barrier(bar_id, EPI_THREADS);
 #pragma unroll
           for (int v = 0; v < 8; ++v)
