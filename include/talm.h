@@ -204,6 +204,52 @@ int talm_head_scale_grad(const void* grad, int64_t ld_grad, int grad_is_f32,
                          const float* grad_loss, const float* denom, int64_t n_rows,
                          int64_t n_cols, void* out, int out_dtype, void* stream);
 
+/* ---- vocabulary-parallel exchange over NVLink peer memory ---------------------------------
+ * No reference counterpart (the reference is single-GPU): these replace the NCCL all_gather of
+ * the statistics and all_reduce of the fp32 gradient of the vocabulary-parallel head.
+ *
+ * Every rank allocates one peer buffer of talm_peer_buffer_size bytes (zero-filled, the same
+ * size on every rank), exports it with talm_ipc_export, exchanges the handles and maps the
+ * other ranks' buffers with talm_ipc_import. `peers` is a device array of `world` uint64 device
+ * addresses: peers[q] = rank q's buffer as mapped in this process (peers[rank] = its own).
+ * `epoch` numbers the call (1, 2, ...; the same on every rank). One call is, in stream order:
+ *   talm_head_publish_stats  -> talm_head_merge_peers -> talm_head_finalize_scatter
+ *   -> talm_head_reduce_gather -> talm_head_gather_finish
+ * Kernels of different ranks wait on each other through flags in the peer buffers; every wait
+ * is bounded (2 s, then TALM_ETIMEOUT in talm_device_status and the kernel returns). */
+#define TALM_IPC_HANDLE_BYTES 64
+int talm_peer_buffer_size(int64_t world, int64_t n_tokens, int64_t hidden, size_t* bytes);
+/* handle: TALM_IPC_HANDLE_BYTES bytes; offset: of ptr within its allocation. */
+int talm_ipc_export(const void* ptr, void* handle, int64_t* offset);
+int talm_ipc_import(const void* handle, int64_t offset, void** ptr);
+int talm_ipc_close(void* ptr, int64_t offset);
+/* Phase 0: this rank's [n_tokens][TALM_HEAD_STATS] statistics into every rank's buffer. */
+int talm_head_publish_stats(const float* stats, int64_t n_tokens, int64_t hidden, int64_t rank,
+                            int64_t world, const uint64_t* peers, uint32_t epoch, void* stream);
+/* Waits for every rank's statistics, then merges them as talm_head_combine does. */
+int talm_head_merge_peers(int64_t n_tokens, int64_t hidden, int64_t rank, int64_t world,
+                          int64_t n_grad, const void* own_buffer, uint32_t epoch,
+                          float* stats_out, float* acc_scale, void* stream);
+/* talm_head_finalize with the partial fp32 gradient row of output row o sent to rank
+ * o / ceil(n_tokens / world) (phase 1) instead of a local array. */
+int talm_head_finalize_scatter(const float* stats, const int64_t* targets, int64_t n_tokens,
+                               int64_t n_grad, const float* acc, const float* acc_scale,
+                               const uint16_t* weight, int64_t ld_weight, int64_t vocab_col0,
+                               int64_t vocab_cols, int64_t hidden_size,
+                               const int64_t* grad_rows, float* token_loss,
+                               float* token_entropy, int32_t* correct, int64_t rank,
+                               int64_t world, const uint64_t* peers, uint32_t epoch,
+                               void* stream);
+/* Phase 2: waits for every rank's rows, sums the rows this rank owns over the ranks in rank
+ * order (fp32), rounds them to fp16 and writes them into every rank's buffer. */
+int talm_head_reduce_gather(int64_t n_tokens, int64_t hidden, int64_t rank, int64_t world,
+                            const uint64_t* peers, uint32_t epoch, void* stream);
+/* Waits for every rank's rows, then copies the [n_tokens][hidden] fp16 gradient to `out`
+ * (16-byte aligned). */
+int talm_head_gather_finish(int64_t n_tokens, int64_t hidden, int64_t world,
+                            const void* own_buffer, uint32_t epoch, uint16_t* out,
+                            void* stream);
+
 #ifdef __cplusplus
 }
 #endif

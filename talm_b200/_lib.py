@@ -18,6 +18,7 @@ _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _INT = ctypes.c_int
 _SZ = ctypes.c_size_t
+_U32 = ctypes.c_uint32
 
 SIGNATURES = {
     "talm_abi_version": (_INT, []),
@@ -37,7 +38,18 @@ SIGNATURES = {
                                   _P, _P, _P, _P, _INT, _P]),
     "talm_head_combine": (_INT, [_P, _I64, _I64, _I64, _I64, _P, _P, _P]),
     "talm_head_scale_grad": (_INT, [_P, _I64, _INT, _P, _P, _I64, _I64, _P, _INT, _P]),
+    "talm_peer_buffer_size": (_INT, [_I64, _I64, _I64, ctypes.POINTER(_SZ)]),
+    "talm_ipc_export": (_INT, [_P, _P, ctypes.POINTER(_I64)]),
+    "talm_ipc_import": (_INT, [_P, _I64, ctypes.POINTER(_P)]),
+    "talm_ipc_close": (_INT, [_P, _I64]),
+    "talm_head_publish_stats": (_INT, [_P, _I64, _I64, _I64, _I64, _P, _U32, _P]),
+    "talm_head_merge_peers": (_INT, [_I64, _I64, _I64, _I64, _I64, _P, _U32, _P, _P, _P]),
+    "talm_head_finalize_scatter": (_INT, [_P, _P, _I64, _I64, _P, _P, _P, _I64, _I64, _I64,
+                                          _I64, _P, _P, _P, _P, _I64, _I64, _P, _U32, _P]),
+    "talm_head_reduce_gather": (_INT, [_I64, _I64, _I64, _I64, _P, _U32, _P]),
+    "talm_head_gather_finish": (_INT, [_I64, _I64, _I64, _P, _U32, _P, _P]),
 }
+IPC_HANDLE_BYTES = 64
 
 # Mirrors include/talm.h.
 HEAD_STATS = 8

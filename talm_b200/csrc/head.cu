@@ -706,16 +706,33 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
 // ------------------------------------------------------------------------------------------
 // 4. finalize: per-row outputs and the hidden gradient
 // ------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) head_finalize_kernel(
-    const float* __restrict__ stats, const long long* __restrict__ targets, int n_tokens,
+// Where a gradient row goes: the caller's [n, hidden] array (fp16 or fp32), or, under the
+// peer exchange, slot `rank` of the owning rank's receive region (fp32).
+struct GradDest {
+  void* grad;                       // local array (null: no gradient)
+  int grad_f32;
+  const unsigned long long* peers;  // non-null: scatter to the owners
+  size_t recv_off;
+  long long rpr;                    // rows per rank
+  int rank;
+  __device__ __forceinline__ void* row_ptr(long long out, int hidden) const {
+    if (peers == nullptr) {
+      return grad_f32 ? static_cast<void*>(static_cast<float*>(grad) + out * hidden)
+                      : static_cast<void*>(static_cast<__half*>(grad) + out * hidden);
+    }
+    const long long q = out / rpr;
+    float* recv = reinterpret_cast<float*>(peers[q] + recv_off);
+    return recv + (static_cast<long long>(rank) * rpr + (out - q * rpr)) * hidden;
+  }
+};
+
+__device__ __forceinline__ void finalize_row(
+    int row, int lane, const float* __restrict__ stats, const long long* __restrict__ targets,
     int n_grad, const float* __restrict__ acc, const float* __restrict__ acc_scale,
     const __half* __restrict__ weight, long long ld_weight, long long col0, long long vcols,
     int hidden, const long long* __restrict__ grad_rows, float* __restrict__ token_loss,
-    float* __restrict__ token_entropy, int* __restrict__ correct, void* __restrict__ grad,
-    int grad_f32, int vec4) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * 8 + warp;
-  if (row >= n_tokens) return;
+    float* __restrict__ token_entropy, int* __restrict__ correct, const GradDest& dest,
+    int vec4) {
   const float* st = stats + static_cast<long long>(row) * TALM_HEAD_STATS;
   const long long tgt = targets[row];
   const bool labelled = tgt >= 0;
@@ -730,7 +747,9 @@ __global__ void __launch_bounds__(256) head_finalize_kernel(
       correct[out] = (labelled && static_cast<long long>(__float_as_int(st[TALM_STAT_IDX])) == tgt)
                          ? 1 : 0;
   }
-  if (grad == nullptr) return;
+  if (dest.grad == nullptr && dest.peers == nullptr) return;
+  const int grad_f32 = dest.peers != nullptr ? 1 : dest.grad_f32;
+  void* const grow = dest.row_ptr(out, hidden);
   const bool live = labelled && row < n_grad && acc != nullptr;
   const bool own = live && tgt >= col0 && tgt < col0 + vcols;
   const float* arow = acc + static_cast<long long>(row) * hidden;
@@ -754,10 +773,9 @@ __global__ void __launch_bounds__(256) head_finalize_kernel(
       const float g0 = value(a.x, __low2half(w01)), g1 = value(a.y, __high2half(w01));
       const float g2 = value(a.z, __low2half(w23)), g3 = value(a.w, __high2half(w23));
       if (grad_f32) {
-        *reinterpret_cast<float4*>(reinterpret_cast<float*>(grad) + out * hidden + h) =
-            make_float4(g0, g1, g2, g3);
+        *reinterpret_cast<float4*>(static_cast<float*>(grow) + h) = make_float4(g0, g1, g2, g3);
       } else {
-        *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(grad) + out * hidden + h) =
+        *reinterpret_cast<uint2*>(static_cast<__half*>(grow) + h) =
             make_uint2(pack_half2(g0, g1), pack_half2(g2, g3));
       }
     }
@@ -766,11 +784,30 @@ __global__ void __launch_bounds__(256) head_finalize_kernel(
   for (int h = lane; h < hidden; h += 32) {
     const float g = value(live ? arow[h] : 0.0f, own ? wrow[h] : __float2half_rn(0.0f));
     if (grad_f32) {
-      reinterpret_cast<float*>(grad)[out * hidden + h] = g;
+      static_cast<float*>(grow)[h] = g;
     } else {
-      reinterpret_cast<__half*>(grad)[out * hidden + h] = __float2half_rn(g);
+      static_cast<__half*>(grow)[h] = __float2half_rn(g);
     }
   }
+}
+
+// One warp per row. With dest.peers (the peer exchange) the kernel ends phase 1: the last CTA
+// raises this rank's flag on every rank once every gradient row has reached its owner.
+__global__ void __launch_bounds__(256) head_finalize_kernel(
+    const float* __restrict__ stats, const long long* __restrict__ targets, int n_tokens,
+    int n_grad, const float* __restrict__ acc, const float* __restrict__ acc_scale,
+    const __half* __restrict__ weight, long long ld_weight, long long col0, long long vcols,
+    int hidden, const long long* __restrict__ grad_rows, float* __restrict__ token_loss,
+    float* __restrict__ token_entropy, int* __restrict__ correct, GradDest dest, int vec4,
+    peer::PeerLayout L, int world, uint32_t epoch) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row < n_tokens)
+    finalize_row(row, lane, stats, targets, n_grad, acc, acc_scale, weight, ld_weight, col0,
+                 vcols, hidden, grad_rows, token_loss, token_entropy, correct, dest, vec4);
+  if (dest.peers != nullptr)
+    peer::cta_signal_phase(reinterpret_cast<uint8_t*>(dest.peers[dest.rank]), dest.peers,
+                           L.flags, L.counters, 1, dest.rank, world, epoch);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -834,28 +871,40 @@ __global__ void __launch_bounds__(256) head_scale_grad_kernel(
 // ------------------------------------------------------------------------------------------
 // vocabulary-parallel merge of shard statistics
 // ------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) head_merge_shards_kernel(const float* __restrict__ gathered,
+// `wait_own` (the peer exchange): first wait until every rank published its statistics into
+// this rank's peer buffer (phase 0). The gathered records are read with L2-only loads: under
+// the peer exchange other GPUs wrote them while this grid may already run.
+__global__ void __launch_bounds__(256) head_merge_shards_kernel(const float* gathered,
                                                                 int n_shards, int n_tokens,
                                                                 int rank, int n_grad,
                                                                 float* __restrict__ out,
-                                                                float* __restrict__ acc_scale) {
+                                                                float* __restrict__ acc_scale,
+                                                                const uint8_t* wait_own,
+                                                                size_t flags_off,
+                                                                uint32_t epoch) {
+  if (wait_own != nullptr && !peer::cta_wait_phase(wait_own, flags_off, 0, n_shards, epoch))
+    return;
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= n_tokens) return;
   float M = -INFINITY, R = -INFINITY, bv = -INFINITY, zt = 0.0f, hit = 0.0f;
   int bi = 0x7fffffff;
   for (int r = 0; r < n_shards; ++r) {
-    const float* st = gathered + (static_cast<long long>(r) * n_tokens + row) * TALM_HEAD_STATS;
-    M = fmaxf(M, st[TALM_STAT_M]);
-    R = fmaxf(R, st[TALM_STAT_REF]);
-    better_arg(bv, bi, st[TALM_STAT_BEST], __float_as_int(st[TALM_STAT_IDX]));
-    if (st[TALM_STAT_HIT] != 0.0f) { zt = st[TALM_STAT_ZT]; hit = 1.0f; }
+    const float4* st4 = reinterpret_cast<const float4*>(
+        gathered + (static_cast<long long>(r) * n_tokens + row) * TALM_HEAD_STATS);
+    const float4 a = __ldcg(st4), b = __ldcg(st4 + 1);  // (M, S, T, ZT), (BEST, IDX, HIT, REF)
+    M = fmaxf(M, a.x);
+    R = fmaxf(R, b.w);
+    better_arg(bv, bi, b.x, __float_as_int(b.y));
+    if (b.z != 0.0f) { zt = a.w; hit = 1.0f; }
   }
   float S = 0.0f, T = 0.0f, mine = 0.0f;
   for (int r = 0; r < n_shards; ++r) {
-    const float* st = gathered + (static_cast<long long>(r) * n_tokens + row) * TALM_HEAD_STATS;
-    const float w = ex2((st[TALM_STAT_REF] - R) * kLog2e);
-    S = fmaf(st[TALM_STAT_S], w, S);
-    T = fmaf(st[TALM_STAT_T], w, T);
+    const float4* st4 = reinterpret_cast<const float4*>(
+        gathered + (static_cast<long long>(r) * n_tokens + row) * TALM_HEAD_STATS);
+    const float4 a = __ldcg(st4), b = __ldcg(st4 + 1);
+    const float w = ex2((b.w - R) * kLog2e);
+    S = fmaf(a.y, w, S);
+    T = fmaf(a.z, w, T);
     if (r == rank) mine = w;
   }
   float* o = out + static_cast<long long>(row) * TALM_HEAD_STATS;
@@ -1164,9 +1213,42 @@ int talm_head_finalize(const float* stats, const int64_t* targets, int64_t n_tok
       stats, reinterpret_cast<const long long*>(targets), static_cast<int>(n_tokens),
       static_cast<int>(n_grad), acc, acc_scale, reinterpret_cast<const __half*>(weight),
       ld_weight, vocab_col0, vocab_cols, static_cast<int>(hidden_size),
-      reinterpret_cast<const long long*>(grad_rows), token_loss, token_entropy, correct, grad,
-      grad_is_f32, vec4);
+      reinterpret_cast<const long long*>(grad_rows), token_loss, token_entropy, correct,
+      head::GradDest{grad, grad_is_f32, nullptr, 0, 1, 0}, vec4, peer::PeerLayout{}, 1, 0u);
   return check_launch("head finalize kernel");
+}
+
+int talm_head_finalize_scatter(const float* stats, const int64_t* targets, int64_t n_tokens,
+                               int64_t n_grad, const float* acc, const float* acc_scale,
+                               const uint16_t* weight, int64_t ld_weight, int64_t vocab_col0,
+                               int64_t vocab_cols, int64_t hidden_size,
+                               const int64_t* grad_rows, float* token_loss,
+                               float* token_entropy, int32_t* correct, int64_t rank,
+                               int64_t world, const uint64_t* peers, uint32_t epoch,
+                               void* stream) {
+  using namespace talm;
+  if (n_tokens < 0 || n_grad < 0 || n_grad > n_tokens)
+    return set_error(TALM_EINVAL, "need 0 <= n_grad <= n_tokens");
+  int st = peer::check_peer_args(world, rank, n_tokens, hidden_size);
+  if (st != TALM_OK) return st;
+  if (!peers || (n_tokens > 0 && (!stats || !targets)) ||
+      (n_grad > 0 && (!acc || !acc_scale || !weight)))
+    return set_error(TALM_EINVAL, "null pointer");
+  const peer::PeerLayout L = peer::peer_layout(world, n_tokens, hidden_size);
+  auto aligned = [](const void* q, uintptr_t a) { return (reinterpret_cast<uintptr_t>(q) & (a - 1)) == 0; };
+  const int vec4 = ld_weight % 4 == 0 && aligned(acc, 16) && aligned(weight, 8);
+  // every CTA takes part in the phase signal, so the grid is never empty
+  const int grid = static_cast<int>(n_tokens > 0 ? (n_tokens + 7) / 8 : 1);
+  LaunchTimer timer(TALM_KERNEL_HEAD_FINALIZE, static_cast<cudaStream_t>(stream));
+  head::head_finalize_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      stats, reinterpret_cast<const long long*>(targets), static_cast<int>(n_tokens),
+      static_cast<int>(n_grad), acc, acc_scale, reinterpret_cast<const __half*>(weight),
+      ld_weight, vocab_col0, vocab_cols, static_cast<int>(hidden_size),
+      reinterpret_cast<const long long*>(grad_rows), token_loss, token_entropy, correct,
+      head::GradDest{nullptr, 1, reinterpret_cast<const unsigned long long*>(peers), L.recv,
+                     L.rpr, static_cast<int>(rank)},
+      vec4, L, static_cast<int>(world), epoch);
+  return check_launch("head finalize scatter kernel");
 }
 
 int talm_head_scale_grad(const void* grad, int64_t ld_grad, int grad_is_f32,
@@ -1221,12 +1303,35 @@ int talm_head_combine(const float* gathered, int64_t n_shards, int64_t n_tokens,
     return set_error(TALM_EINVAL, "bad shard arguments");
   if (n_tokens == 0) return TALM_OK;
   if (!gathered || !stats_out) return set_error(TALM_EINVAL, "null pointer");
+  if ((reinterpret_cast<uintptr_t>(gathered) & 15) != 0)
+    return set_error(TALM_EINVAL, "gathered statistics must be 16-byte aligned");
   LaunchTimer timer(TALM_KERNEL_HEAD_MERGE, static_cast<cudaStream_t>(stream));
   head::head_merge_shards_kernel<<<static_cast<int>((n_tokens + 255) / 256), 256, 0,
                                    static_cast<cudaStream_t>(stream)>>>(
       gathered, static_cast<int>(n_shards), static_cast<int>(n_tokens), static_cast<int>(rank),
-      static_cast<int>(n_grad), stats_out, acc_scale);
+      static_cast<int>(n_grad), stats_out, acc_scale, nullptr, 0, 0u);
   return check_launch("head merge kernel");
+}
+
+int talm_head_merge_peers(int64_t n_tokens, int64_t hidden, int64_t rank, int64_t world,
+                          int64_t n_grad, const void* own_buffer, uint32_t epoch,
+                          float* stats_out, float* acc_scale, void* stream) {
+  using namespace talm;
+  int st = peer::check_peer_args(world, rank, n_tokens, hidden);
+  if (st != TALM_OK) return st;
+  if (n_grad < 0 || n_grad > n_tokens) return set_error(TALM_EINVAL, "need 0 <= n_grad <= n_tokens");
+  if (n_tokens == 0) return TALM_OK;
+  if (!own_buffer || !stats_out || (n_grad > 0 && !acc_scale))
+    return set_error(TALM_EINVAL, "null pointer");
+  const peer::PeerLayout L = peer::peer_layout(world, n_tokens, hidden);
+  const uint8_t* own = static_cast<const uint8_t*>(own_buffer);
+  LaunchTimer timer(TALM_KERNEL_HEAD_MERGE, static_cast<cudaStream_t>(stream));
+  head::head_merge_shards_kernel<<<static_cast<int>((n_tokens + 255) / 256), 256, 0,
+                                   static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const float*>(own + L.stats), static_cast<int>(world),
+      static_cast<int>(n_tokens), static_cast<int>(rank), static_cast<int>(n_grad), stats_out,
+      acc_scale, own, L.flags, epoch);
+  return check_launch("head merge peers kernel");
 }
 
 }  // extern "C"

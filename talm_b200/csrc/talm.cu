@@ -2,5 +2,6 @@
 // one module, so no relocatable device code is needed.
 #include "abi.cu"
 #include "nf4.cu"
+#include "peer.cu"
 #include "head.cu"
 #include "head_noalloc.cu"

@@ -7,17 +7,27 @@ weight rows [col0_r, col0_r + cols_r). Every rank holds the full hidden states a
   1. each rank runs the sm_100a head over its rows (`talm_head_shard`): per-row statistics
      (m_r, s_r, t_r, z_target if owned, first argmax) and the accumulator
      acc_r = sum_{v in shard} exp(z_v - m_r) W[v] of the labelled rows;
-  2. all_gather of the [N, 8] fp32 statistics (16 bytes of payload per row and rank);
-  3. each rank merges them locally and deterministically (`talm_head_combine`): M = max m_r,
-     S = sum s_r e^{m_r - M}, T likewise, argmax = the first column among the shards' maxima,
-     and its own accumulator scale e^{m_r - M} / S;
-  4. `talm_head_finalize` writes the per-row outputs (identical on every rank) and the rank's
-     partial gradient acc_r * scale_r - [target owned] W[target] in fp32;
-  5. all_reduce(SUM) of the [N, H] fp32 partial gradients.
+  2. every rank's [N, 8] fp32 statistics reach every rank;
+  3. each rank merges them locally and deterministically: M = max m_r, S = sum s_r e^{m_r - M},
+     T likewise, argmax = the first column among the shards' maxima, and its own accumulator
+     scale e^{m_r - M} / S;
+  4. the per-row outputs (identical on every rank) and the rank's partial gradient
+     acc_r * scale_r - [target owned] W[target] in fp32;
+  5. the partial gradients are summed over the ranks.
 
-The kernels and the collectives are behind `HeadOps` so that the exchange logic can be exercised
-with CPU ranks (gloo) by the tests; the product path is `CudaHeadOps`.
+On CUDA ranks that can map each other's memory (one node, NVLink) steps 2-5 run as the peer
+exchange of the library (`PeerExchange`, talm_head_publish_stats ... talm_head_gather_finish):
+kernels write the statistics and the gradient rows straight into the other GPUs' buffers, each
+row is reduced once by its owner and the fp16 result is written to every rank. Otherwise
+(TALM_B200_PEER_EXCHANGE=0, or ranks that cannot map each other's memory) step 2 is an NCCL
+all_gather and step 5 an all_reduce of the fp32 gradient.
+
+The kernels are behind `HeadOps` so that the collective flow can be exercised with CPU ranks
+(gloo) by the tests; the product path is `CudaHeadOps`.
 """
+
+import ctypes
+import os
 
 import torch
 import torch.distributed as dist
@@ -85,13 +95,135 @@ class CudaHeadOps:
 
 OPS = CudaHeadOps()
 
+PEER_EXCHANGE = os.environ.get("TALM_B200_PEER_EXCHANGE", "1") != "0"
+
+
+class PeerExchange:
+    """One rank's peer buffer and its mappings of the other ranks' buffers (CUDA IPC), for one
+    process group and device. The buffer grows (in lockstep on every rank: the sizes depend only
+    on replicated shapes) when a call needs more. `ok` is False when some rank could not map
+    the others' memory; the caller then uses the NCCL flow."""
+
+    def __init__(self, group, device):
+        self.group, self.device = group, device
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.size = 0
+        self.buf = None
+        self.mapped = []      # (pointer, offset) of the imported peer buffers
+        self.peers = None     # device int64 [world]: every rank's buffer in this process
+        self.epoch = 0
+        self.ok = True
+
+    def _release(self):
+        lib = _lib.load()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # no rank still writes into the old buffers
+        for p, off in self.mapped:
+            lib.talm_ipc_close(p, off)
+        self.mapped, self.buf, self.peers = [], None, None
+
+    def ensure(self, n_tokens, hidden_cols):
+        lib = _lib.load()
+        need = _lib._SZ(0)
+        _lib.check(lib.talm_peer_buffer_size(self.world, n_tokens, hidden_cols, need),
+                   "talm_peer_buffer_size")
+        if self.buf is not None and need.value <= self.size:
+            return self.ok
+        if self.buf is not None:
+            self._release()
+        self.size = max(need.value, 2 * self.size)
+        self.buf = torch.zeros(self.size, dtype=torch.uint8, device=self.device)
+        handle = (ctypes.c_ubyte * _lib.IPC_HANDLE_BYTES)()
+        offset = _lib._I64(0)
+        _lib.check(lib.talm_ipc_export(_lib.ptr(self.buf), ctypes.cast(handle, ctypes.c_void_p),
+                                       ctypes.byref(offset)), "talm_ipc_export")
+        mine = torch.tensor(list(bytes(handle)) + list(offset.value.to_bytes(8, "little")),
+                            dtype=torch.uint8, device=self.device)
+        everyone = torch.empty(self.world * mine.numel(), dtype=torch.uint8, device=self.device)
+        dist.all_gather_into_tensor(everyone, mine, group=self.group)
+        records = everyone.view(self.world, -1).cpu()
+        addrs, good = [], 1
+        for q in range(self.world):
+            if q == self.rank:
+                addrs.append(self.buf.data_ptr())
+                continue
+            raw = bytes(records[q].tolist())
+            h = (ctypes.c_ubyte * _lib.IPC_HANDLE_BYTES).from_buffer_copy(raw[:_lib.IPC_HANDLE_BYTES])
+            off = int.from_bytes(raw[_lib.IPC_HANDLE_BYTES:], "little")
+            p = ctypes.c_void_p(0)
+            if lib.talm_ipc_import(ctypes.cast(h, ctypes.c_void_p), off, ctypes.byref(p)) != 0:
+                good = 0
+                addrs.append(0)
+                continue
+            self.mapped.append((p.value, off))
+            addrs.append(p.value)
+        flag = torch.tensor([good], dtype=torch.int32, device=self.device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.group)
+        self.ok = bool(flag.item())
+        self.peers = torch.tensor(addrs, dtype=torch.int64, device=self.device)
+        return self.ok
+
+    def next_epoch(self):
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
+        return self.epoch
+
+
+_EXCHANGES = {}
+
+
+def _exchange(group, device, n_tokens, hidden_cols):
+    key = (id(group) if group is not None else None, device.index)
+    ex = _EXCHANGES.get(key)
+    if ex is None:
+        ex = _EXCHANGES[key] = PeerExchange(group, device)
+    return ex if ex.ensure(n_tokens, hidden_cols) else None
+
+
+def _peer_flow(ex, stats, acc, rows_targets, n_grad, w16, ld_w, col0, cols, src, need_grad):
+    """Steps 2-5 through the peer buffers: returns token_loss, token_entropy, correct (int32)
+    and the reduced fp16 gradient [N, cols] (or None)."""
+    lib = _lib.load()
+    device = stats.device
+    stream = _lib.stream_of(device)
+    n_tokens = stats.shape[0]
+    epoch = ex.next_epoch()
+    peers, own = _lib.ptr(ex.peers), _lib.ptr(ex.buf)
+    _lib.check(lib.talm_head_publish_stats(_lib.ptr(stats), n_tokens, cols, ex.rank, ex.world,
+                                           peers, epoch, stream), "talm_head_publish_stats")
+    merged = torch.empty(n_tokens, _lib.HEAD_STATS, dtype=torch.float32, device=device)
+    scale = torch.empty(max(n_grad, 1), dtype=torch.float32, device=device)
+    _lib.check(lib.talm_head_merge_peers(n_tokens, cols, ex.rank, ex.world, n_grad, own, epoch,
+                                         _lib.ptr(merged), _lib.ptr(scale), stream),
+               "talm_head_merge_peers")
+    token_loss = torch.empty(n_tokens, dtype=torch.float32, device=device)
+    token_entropy = torch.empty_like(token_loss)
+    correct = torch.empty(n_tokens, dtype=torch.int32, device=device)
+    if not need_grad:
+        _lib.check(lib.talm_head_finalize(
+            _lib.ptr(merged), _lib.ptr(rows_targets), n_tokens, 0, None, None, _lib.ptr(w16),
+            ld_w, col0, w16.shape[0], cols, _lib.ptr(src), _lib.ptr(token_loss),
+            _lib.ptr(token_entropy), _lib.ptr(correct), None, 0, stream), "talm_head_finalize")
+        return token_loss, token_entropy, correct, None
+    _lib.check(lib.talm_head_finalize_scatter(
+        _lib.ptr(merged), _lib.ptr(rows_targets), n_tokens, n_grad, _lib.ptr(acc),
+        _lib.ptr(scale), _lib.ptr(w16), ld_w, col0, w16.shape[0], cols, _lib.ptr(src),
+        _lib.ptr(token_loss), _lib.ptr(token_entropy), _lib.ptr(correct), ex.rank, ex.world,
+        peers, epoch, stream), "talm_head_finalize_scatter")
+    _lib.check(lib.talm_head_reduce_gather(n_tokens, cols, ex.rank, ex.world, peers, epoch,
+                                           stream), "talm_head_reduce_gather")
+    grad = torch.empty(n_tokens, cols, dtype=torch.float16, device=device)
+    _lib.check(lib.talm_head_gather_finish(n_tokens, cols, ex.world, own, epoch,
+                                           _lib.ptr(grad), stream), "talm_head_gather_finish")
+    return token_loss, token_entropy, correct, grad
+
 
 def sharded_head(hidden, weight_shard, targets, vocab, col0, num_items=None, vocab_chunk=8192,
                  need_grad=True, n_labelled=None, group=None, ops=None):
     """One rank's part of the vocabulary-parallel head. Returns (loss, token_loss, entropy,
-    correct, grad_hidden) with grad_hidden the all-reduced dH in fp32 (unscaled by the loss
-    denominator; the backward rounds it to fp16, the value the single-GPU head saves) or None;
-    every rank gets the same values."""
+    correct, grad_hidden) with grad_hidden the summed dH (unscaled by the loss denominator;
+    fp16 from the peer exchange, fp32 from the NCCL flow, which the backward rounds to fp16 as
+    the single-GPU head saves it) or None; every rank gets the same values."""
     ops = ops or OPS
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
@@ -112,6 +244,17 @@ def sharded_head(hidden, weight_shard, targets, vocab, col0, num_items=None, voc
             rows_targets = targets.index_select(0, src)
 
     stats, acc = ops.shard(h16, w16, ld_w, rows_targets, n_grad, cols, col0, int(vocab_chunk))
+    ex = (_exchange(group, stats.device, n_tokens, cols)
+          if PEER_EXCHANGE and isinstance(ops, CudaHeadOps) and world > 1 and n_tokens > 0
+          else None)
+    if ex is not None:
+        token_loss, token_entropy, correct, grad = _peer_flow(
+            ex, stats, acc, rows_targets, n_grad, w16, ld_w, col0, cols, src, need_grad)
+        if grad is not None:
+            grad = grad[:, :hidden_size]
+        denom = _denominator(num_items, labelled.sum())
+        loss = token_loss.sum() / denom
+        return loss, token_loss, token_entropy, correct.to(torch.bool), grad
     gathered = torch.empty(world * n_tokens, _lib.HEAD_STATS, dtype=torch.float32,
                            device=stats.device)
     dist.all_gather_into_tensor(gathered, stats, group=group)

@@ -30,7 +30,7 @@ def _case(n, vocab, size, device):
     return hidden, weight, targets
 
 
-def _worker(rank, world, port, q, n, vocab, size):
+def _worker(rank, world, port, q, sizes, vocab, size, peer):
     import datetime
 
     import torch.distributed as dist
@@ -41,34 +41,43 @@ def _worker(rank, world, port, q, n, vocab, size):
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                             timeout=datetime.timedelta(seconds=120))
     try:
+        from talm_b200 import vocab_parallel
         from talm_b200.fused_head import fused_head_loss
         from talm_b200.vocab_parallel import shard_bounds, vocab_parallel_head_loss
 
-        hidden, weight, targets = _case(n, vocab, size, dev)
+        vocab_parallel.PEER_EXCHANGE = peer
         col0, cols = shard_bounds(vocab, world, rank)
-        x = hidden.clone().requires_grad_(True)
-        out = vocab_parallel_head_loss(x, weight[col0:col0 + cols], targets, vocab, col0, None,
-                                       2048)
-        (out[0] * 7.0).backward()
-        y = hidden.clone().requires_grad_(True)
-        ref = fused_head_loss(y, weight, targets, None, 2048)
-        (ref[0] * 7.0).backward()
-        q.put((rank, [t.detach().cpu() for t in out], x.grad.cpu(),
-               [t.detach().cpu() for t in ref], y.grad.cpu()))
+        results = []
+        # several calls: the peer buffers are reused (epochs) and grow once (600 -> 1500 rows)
+        for n in sizes:
+            hidden, weight, targets = _case(n, vocab, size, dev)
+            x = hidden.clone().requires_grad_(True)
+            out = vocab_parallel_head_loss(x, weight[col0:col0 + cols], targets, vocab, col0,
+                                           None, 2048)
+            (out[0] * 7.0).backward()
+            y = hidden.clone().requires_grad_(True)
+            ref = fused_head_loss(y, weight, targets, None, 2048)
+            (ref[0] * 7.0).backward()
+            results.append(([t.detach().cpu() for t in out], x.grad.cpu(),
+                            [t.detach().cpu() for t in ref], y.grad.cpu()))
+        from talm_b200 import _lib
+        q.put((rank, results, _lib.device_status()))
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-def test_vocab_parallel_matches_single_gpu():
+@pytest.mark.parametrize("peer", [True, False], ids=["peer-exchange", "nccl"])
+def test_vocab_parallel_matches_single_gpu(peer):
+    """Both exchange flows: the library's NVLink peer exchange and NCCL collectives."""
     world = min(torch.cuda.device_count(), 4)
     if world < 2:
         pytest.skip("needs 2 or more GPUs")
-    n, vocab, size = 600, 30011, 512
+    sizes, vocab, size = (600, 1500, 600), 30011, 512
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, n, vocab, size))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, sizes, vocab, size, peer))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -76,12 +85,14 @@ def test_vocab_parallel_matches_single_gpu():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for rank, out, grad, ref, ref_grad in results:
-        loss, token_loss, entropy, correct = out
-        r_loss, r_tl, r_ent, r_corr = ref
-        torch.testing.assert_close(loss, r_loss, rtol=1e-5, atol=1e-6)
-        torch.testing.assert_close(token_loss, r_tl, rtol=1e-5, atol=1e-5)
-        torch.testing.assert_close(entropy, r_ent, rtol=1e-5, atol=1e-5)
-        assert torch.equal(correct, r_corr), f"rank {rank}"
-        torch.testing.assert_close(grad.float(), ref_grad.float(), rtol=1e-3,
-                                   atol=float(ref_grad.abs().max()) * 2 ** -10)
+    for rank, calls, status in results:
+        assert status == 0, f"rank {rank}: device status {status}"
+        for out, grad, ref, ref_grad in calls:
+            loss, token_loss, entropy, correct = out
+            r_loss, r_tl, r_ent, r_corr = ref
+            torch.testing.assert_close(loss, r_loss, rtol=1e-5, atol=1e-6)
+            torch.testing.assert_close(token_loss, r_tl, rtol=1e-5, atol=1e-5)
+            torch.testing.assert_close(entropy, r_ent, rtol=1e-5, atol=1e-5)
+            assert torch.equal(correct, r_corr), f"rank {rank}"
+            torch.testing.assert_close(grad.float(), ref_grad.float(), rtol=1e-3,
+                                       atol=float(ref_grad.abs().max()) * 2 ** -10)
