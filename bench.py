@@ -122,17 +122,26 @@ def max_over_ranks(value, world):
     return float(t.item())
 
 
-def timed(fn, steps, world):
+HOST_MS = {}  # host time to issue the timed loop, per timed() label (diagnostic only)
+
+
+def timed(fn, steps, world, label=None):
     """Device time of `steps` calls of fn (CUDA events on the current stream, barrier and
-    synchronize on both sides), max over ranks, in ms."""
+    synchronize on both sides), max over ranks, in ms. With `label`, the host time spent
+    issuing the loop (before the closing synchronize) is kept in HOST_MS: when it is close to
+    the device time, the step is bound by the host, not the GPU."""
     barrier(world)
     start = torch.cuda.Event(enable_timing=True)
     stop = torch.cuda.Event(enable_timing=True)
     start.record()
+    t0 = time.perf_counter()
     for _ in range(steps):
         fn()
+    host = (time.perf_counter() - t0) * 1000
     stop.record()
     barrier(world)
+    if label is not None:
+        HOST_MS[label] = max_over_ranks(host, world) / steps
     return max_over_ranks(start.elapsed_time(stop), world)
 
 
@@ -290,11 +299,11 @@ def run_head(world, rank, local, steps, warmup, hidden, weight, targets, clocks_
     for _ in range(warmup):
         step()
     sampler = ClockSampler(clocks_on and rank == 0)
-    ms = timed(step, steps, world)
+    ms = timed(step, steps, world, "head")
     clocks = sampler.stop(set(range(world))) if rank == 0 else None
     prof = profile_kernels(step, steps)
     return {"ms_per_step": ms / steps, "n_tokens": n_tokens, "n_labelled": n_lab,
-            "clocks": clocks, "kernels": prof}
+            "clocks": clocks, "kernels": prof, "host_ms_per_step": HOST_MS.get("head")}
 
 
 def run_head_e2e(world, rank, steps, warmup, hidden, weight, targets):
@@ -474,6 +483,7 @@ def ours(args, world, rank, local):
         "clocks": head["clocks"],
         "kernels": {k: {"ms_per_step": v[0] / args.steps, "launches_per_step": v[1] / args.steps,
                         "share": v[0] / total_ms} for k, v in kernels.items() if v[1]},
+        "host_ms_per_step": head["host_ms_per_step"],
     }
     del hidden
     if not args.no_secondary:

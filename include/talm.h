@@ -61,7 +61,10 @@ int talm_device_status(int* status_out);
 #define TALM_KERNEL_NF4 5           /* nf4 bulk-copy and chunk kernels (main body)        */
 #define TALM_KERNEL_NF4_TAIL 6      /* nf4 byte kernel (tails, unaligned pointers)        */
 #define TALM_KERNEL_HEAD_SCALE 7    /* head_scale_grad_kernel (backward scaling)          */
-#define TALM_KERNEL_KINDS 8
+#define TALM_KERNEL_PEER_PUBLISH 8  /* publish_stats_kernel (peer exchange, phase 0)      */
+#define TALM_KERNEL_PEER_REDUCE 9   /* reduce_gather_kernel (peer exchange, phase 2)      */
+#define TALM_KERNEL_PEER_FINISH 10  /* gather_finish_kernel (wait + copy out)             */
+#define TALM_KERNEL_KINDS 11
 int talm_profile_begin(void);
 int talm_profile_end(double* ms_out, int64_t* launches_out, int n_kinds);
 
@@ -230,8 +233,9 @@ int talm_head_publish_stats(const float* stats, int64_t n_tokens, int64_t hidden
 int talm_head_merge_peers(int64_t n_tokens, int64_t hidden, int64_t rank, int64_t world,
                           int64_t n_grad, const void* own_buffer, uint32_t epoch,
                           float* stats_out, float* acc_scale, void* stream);
-/* talm_head_finalize with the partial fp32 gradient row of output row o sent to rank
- * o / ceil(n_tokens / world) (phase 1) instead of a local array. */
+/* talm_head_finalize with the partial fp32 gradient row of output row o stored by the kernel
+ * straight into the buffer of rank o / ceil(n_tokens / world) (phase 1) instead of a local
+ * array. */
 int talm_head_finalize_scatter(const float* stats, const int64_t* targets, int64_t n_tokens,
                                int64_t n_grad, const float* acc, const float* acc_scale,
                                const uint16_t* weight, int64_t ld_weight, int64_t vocab_col0,

@@ -99,7 +99,7 @@ def stream_of(device):
 
 
 KERNEL_KINDS = ("head_logits", "head_combine", "head_accum", "head_finalize", "head_merge",
-                "nf4", "nf4_tail", "head_scale")
+                "nf4", "nf4_tail", "head_scale", "peer_publish", "peer_reduce", "peer_finish")
 
 
 def profile_begin():

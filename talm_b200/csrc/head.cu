@@ -29,6 +29,7 @@
 // writing rows in the caller's original order.
 #include <math.h>
 
+#include <algorithm>
 #include <mutex>
 #include <type_traits>
 
@@ -1239,8 +1240,9 @@ int talm_head_finalize_scatter(const float* stats, const int64_t* targets, int64
   const int vec4 = ld_weight % 4 == 0 && aligned(acc, 16) && aligned(weight, 8);
   // every CTA takes part in the phase signal, so the grid is never empty
   const int grid = static_cast<int>(n_tokens > 0 ? (n_tokens + 7) / 8 : 1);
-  LaunchTimer timer(TALM_KERNEL_HEAD_FINALIZE, static_cast<cudaStream_t>(stream));
-  head::head_finalize_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LaunchTimer timer(TALM_KERNEL_HEAD_FINALIZE, s);
+  head::head_finalize_kernel<<<grid, 256, 0, s>>>(
       stats, reinterpret_cast<const long long*>(targets), static_cast<int>(n_tokens),
       static_cast<int>(n_grad), acc, acc_scale, reinterpret_cast<const __half*>(weight),
       ld_weight, vocab_col0, vocab_cols, static_cast<int>(hidden_size),

@@ -26,6 +26,8 @@
 // waiting CTA polls its own flags with acquire loads; every wait is bounded (kWaitLimitNs) and
 // records TALM_ETIMEOUT on expiry, after which the kernel returns without its work. Data that
 // other GPUs write while a kernel runs is read with L2-only loads (__ldcg).
+#include <string.h>
+
 #include "common.cuh"
 
 namespace talm {
@@ -268,6 +270,7 @@ int talm_head_publish_stats(const float* stats, int64_t n_tokens, int64_t hidden
   if (!peers || (n_tokens > 0 && !stats)) return set_error(TALM_EINVAL, "null pointer");
   const peer::PeerLayout L = peer::peer_layout(world, n_tokens, hidden);
   const long long n4 = n_tokens * (TALM_HEAD_STATS / 4);
+  LaunchTimer timer(TALM_KERNEL_PEER_PUBLISH, static_cast<cudaStream_t>(stream));
   peer::publish_stats_kernel<<<peer::grid_for(n4), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const float4*>(stats), n4,
       reinterpret_cast<const unsigned long long*>(peers), L, static_cast<int>(rank),
@@ -283,6 +286,7 @@ int talm_head_reduce_gather(int64_t n_tokens, int64_t hidden, int64_t rank, int6
   if (!peers) return set_error(TALM_EINVAL, "null pointer");
   const peer::PeerLayout L = peer::peer_layout(world, n_tokens, hidden);
   const long long items = L.rpr * (hidden / 8);
+  LaunchTimer timer(TALM_KERNEL_PEER_REDUCE, static_cast<cudaStream_t>(stream));
   peer::reduce_gather_kernel<<<peer::grid_for(items), 256, 0,
                                static_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const unsigned long long*>(peers), L, static_cast<int>(rank),
@@ -301,6 +305,7 @@ int talm_head_gather_finish(int64_t n_tokens, int64_t hidden, int64_t world,
     return set_error(TALM_EINVAL, "out must be 16-byte aligned");
   const peer::PeerLayout L = peer::peer_layout(world, n_tokens, hidden);
   const long long n16 = n_tokens * hidden / 8;
+  LaunchTimer timer(TALM_KERNEL_PEER_FINISH, static_cast<cudaStream_t>(stream));
   peer::gather_finish_kernel<<<peer::grid_for(n16), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint8_t*>(own_buffer), L, static_cast<int>(world), n16, epoch,
       reinterpret_cast<uint4*>(out));

@@ -30,7 +30,7 @@ def _case(n, vocab, size, device):
     return hidden, weight, targets
 
 
-def _worker(rank, world, port, q, sizes, vocab, size, peer):
+def _worker(rank, world, port, q, sizes, vocab, size, flow):
     import datetime
 
     import torch.distributed as dist
@@ -45,7 +45,7 @@ def _worker(rank, world, port, q, sizes, vocab, size, peer):
         from talm_b200.fused_head import fused_head_loss
         from talm_b200.vocab_parallel import shard_bounds, vocab_parallel_head_loss
 
-        vocab_parallel.PEER_EXCHANGE = peer
+        vocab_parallel.PEER_EXCHANGE = flow != "nccl"
         col0, cols = shard_bounds(vocab, world, rank)
         results = []
         # several calls: the peer buffers are reused (epochs) and grow once (600 -> 1500 rows)
@@ -67,8 +67,8 @@ def _worker(rank, world, port, q, sizes, vocab, size, peer):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("peer", [True, False], ids=["peer-exchange", "nccl"])
-def test_vocab_parallel_matches_single_gpu(peer):
+@pytest.mark.parametrize("flow", ["peer", "nccl"])
+def test_vocab_parallel_matches_single_gpu(flow):
     """Both exchange flows: the library's NVLink peer exchange and NCCL collectives."""
     world = min(torch.cuda.device_count(), 4)
     if world < 2:
@@ -77,7 +77,7 @@ def test_vocab_parallel_matches_single_gpu(peer):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, sizes, vocab, size, peer))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, sizes, vocab, size, flow))
              for r in range(world)]
     for p in procs:
         p.start()
