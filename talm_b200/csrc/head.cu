@@ -940,11 +940,37 @@ inline int64_t chunk_cols(int64_t vocab_cols, int64_t vocab_chunk) {
   return c < BN ? BN : c;
 }
 
+// Width of the first slice. Every row's reference REF is set from the first slice, which has
+// no reference to work against: its probabilities are taken relative to each 128-column part's
+// own max and rescaled in place by the combine kernel (read + write of the slice's fp16
+// probability rows). A narrow first slice keeps that pass small (2048 columns of 16384 rows:
+// 67 MB, L2-resident); the later slices then run against REF and move it only when a row's
+// max outgrows REF + kRefSlack.
+constexpr int64_t kFirstSliceCols = 2048;
+
+// The slices of a walk over `vocab_cols` columns: a first slice of at most kFirstSliceCols,
+// then the rest in equal slices of whole tiles, none wider than `chunk` (no narrow tail slice).
+struct Slices {
+  int64_t first, width, count;
+  int64_t begin(int64_t k) const { return k == 0 ? 0 : first + (k - 1) * width; }
+};
+
+inline Slices slices_of(int64_t vocab_cols, int64_t chunk) {
+  Slices s;
+  s.first = std::min<int64_t>(std::min<int64_t>(kFirstSliceCols, chunk), vocab_cols);
+  s.first = (s.first + BN - 1) / BN * BN;
+  const int64_t rest = vocab_cols > s.first ? vocab_cols - s.first : 0;
+  const int64_t n_rest = (rest + chunk - 1) / chunk;
+  s.width = n_rest > 0 ? ((rest + n_rest - 1) / n_rest + BN - 1) / BN * BN : chunk;
+  s.count = 1 + n_rest;
+  return s;
+}
+
 Workspace layout(int64_t n_tokens, int64_t n_grad, int64_t vocab_cols, int64_t vocab_chunk,
                  uint8_t* base) {
   const int64_t chunk = chunk_cols(vocab_cols, vocab_chunk);
   const int64_t tiles = chunk / BN * PARTS;  // statistics records per row and slice
-  const int64_t n_slices = (vocab_cols + chunk - 1) / chunk;
+  const int64_t n_slices = slices_of(vocab_cols, chunk).count;
   const int n_buf = n_slices > 1 ? 2 : 1;
   Workspace w;
   size_t off = 0;
@@ -1091,7 +1117,8 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
     st = talm_make_tmap_2d_f32(&tm_acc, acc, hidden_size, n_grad, hidden_size, 32, BM);
   if (st != TALM_OK) return st;
 
-  const int64_t n_slices = (vocab_cols + chunk - 1) / chunk;
+  const Slices sl = slices_of(vocab_cols, chunk);
+  const int64_t n_slices = sl.count;
   std::lock_guard<std::mutex> lock(g_pipe_mutex);
   // The accumulator GEMM goes to the side stream (overlapping the next slice's logits GEMM)
   // only when it has fewer tiles than the GPU has SMs; a GEMM that fills the GPU on its own
@@ -1113,9 +1140,10 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
   const int n_pair_rows = static_cast<int>((n_tokens + PAIR_ROWS - 1) / PAIR_ROWS);
   const int max_pairs = max_pairs_of(sms);
   for (int64_t k = 0; k < n_slices; ++k) {
-    const int64_t s0 = k * chunk;
+    const int64_t s0 = sl.begin(k);
     const int buf = static_cast<int>(k & 1);
-    const int cols = static_cast<int>(vocab_cols - s0 < chunk ? vocab_cols - s0 : chunk);
+    const int64_t s1 = std::min<int64_t>(vocab_cols, k == 0 ? sl.first : s0 + sl.width);
+    const int cols = static_cast<int>(s1 - s0);
     const int n_col_tiles = (cols + BN - 1) / BN;
     // the pair of buffers this slice writes is free once slice k - 2's accumulator GEMM is done
     if (pipe && k >= 2 && cudaStreamWaitEvent(stream, pipe->drained[buf], 0) != cudaSuccess)
