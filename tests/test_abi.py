@@ -85,3 +85,30 @@ def test_workspace_size_is_host_only(lib):
     # a single slice needs a single buffer
     assert lib.talm_head_workspace_size(64, 64, 64, 1000, 8192, ctypes.byref(size)) == 0
     assert 64 * 1024 * 2 < size.value < 2 * 64 * 1024 * 2
+
+
+def test_peer_buffer_layout_is_host_only(lib):
+    """The peer-exchange buffer holds flags, every rank's statistics, the fp32 rows the rank
+    owns from every rank and the fp16 gradient: at config 4 on 8 GPUs about 154 MB."""
+    size = ctypes.c_size_t(0)
+    n, h, w = 16384, 1536, 8
+    assert lib.talm_peer_buffer_size(w, n, h, ctypes.byref(size)) == 0
+    payload = w * n * 8 * 4 + w * (n // w) * h * 4 + n * h * 2
+    assert payload < size.value < payload + 8192
+    # rows per rank round up: every row has an owner
+    assert lib.talm_peer_buffer_size(3, 10, 8, ctypes.byref(size)) == 0
+    assert size.value >= 3 * 4 * 8 * 4 + 10 * 8 * 2
+    # hidden columns must be a multiple of 8, rank inside the group
+    assert lib.talm_peer_buffer_size(2, 10, 12, ctypes.byref(size)) == 1
+    assert lib.talm_peer_buffer_size(0, 10, 8, ctypes.byref(size)) == 1
+
+
+def test_peer_exchange_and_backward_reject_bad_arguments(lib):
+    assert lib.talm_head_publish_stats(None, 4, 8, 2, 2, None, 1, None) == 1    # rank >= world
+    assert lib.talm_head_reduce_gather(4, 8, 0, 2, None, 1, None) == 1          # no peer table
+    assert lib.talm_head_gather_finish(4, 8, 2, None, 1, None, None) == 1
+    assert lib.talm_ipc_export(None, None, None) == 1
+    # backward: out_dtype outside TALM_DTYPE_*, a row stride shorter than the row
+    assert lib.talm_head_scale_grad(None, 8, 0, None, None, 4, 8, None, 7, None) == 1
+    assert lib.talm_head_scale_grad(None, 4, 0, None, None, 4, 8, None, 0, None) == 1
+    assert lib.talm_head_scale_grad(None, 8, 0, None, None, 0, 8, None, 0, None) == 0
