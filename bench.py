@@ -163,9 +163,18 @@ class ClockSampler:
             self.out = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=self.out, stderr=subprocess.DEVNULL)
+                 "-lms", "25"], stdout=self.out, stderr=subprocess.DEVNULL)
         except Exception:  # noqa: BLE001 - no nvidia-smi: no clock record
             self.proc = None
+            return
+        # the timed region starts once the sampler is producing samples (nvidia-smi takes a
+        # moment to start), so that the record covers it
+        deadline = time.time() + 5.0
+        while time.time() < deadline and self.proc.poll() is None:
+            self.out.flush()
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.02)
 
     def stop(self, gpus):
         if self.proc is None:
@@ -292,6 +301,30 @@ def profile_kernels(fn, steps):
     return _lib.profile_end()
 
 
+def graph_ms_per_step(step, steps, warmup):
+    """Device time per step of `step` captured once as a CUDA graph and replayed: the same
+    kernels with no host work between them (diagnostic: the gap to the eager step is host
+    overhead). Single GPU only. None when the capture fails."""
+    try:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                step()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        for _ in range(warmup):
+            graph.replay()
+        ms = timed(graph.replay, steps, 1)
+        del graph
+        return ms / steps
+    except Exception as exc:  # noqa: BLE001 - diagnostic only
+        print(f"[bench] graph capture failed: {exc}", file=sys.stderr)
+        return None
+
+
 def run_head(world, rank, local, steps, warmup, hidden, weight, targets, clocks_on):
     n_tokens = hidden.shape[0]
     n_lab = int((targets >= 0).sum())
@@ -302,8 +335,10 @@ def run_head(world, rank, local, steps, warmup, hidden, weight, targets, clocks_
     ms = timed(step, steps, world, "head")
     clocks = sampler.stop(set(range(world))) if rank == 0 else None
     prof = profile_kernels(step, steps)
+    graph = graph_ms_per_step(step, steps, warmup) if world == 1 else None
     return {"ms_per_step": ms / steps, "n_tokens": n_tokens, "n_labelled": n_lab,
-            "clocks": clocks, "kernels": prof, "host_ms_per_step": HOST_MS.get("head")}
+            "clocks": clocks, "kernels": prof, "host_ms_per_step": HOST_MS.get("head"),
+            "graph_ms_per_step": graph}
 
 
 def run_head_e2e(world, rank, steps, warmup, hidden, weight, targets):
@@ -484,6 +519,7 @@ def ours(args, world, rank, local):
         "kernels": {k: {"ms_per_step": v[0] / args.steps, "launches_per_step": v[1] / args.steps,
                         "share": v[0] / total_ms} for k, v in kernels.items() if v[1]},
         "host_ms_per_step": head["host_ms_per_step"],
+        "graph_ms_per_step": head["graph_ms_per_step"],
     }
     del hidden
     if not args.no_secondary:
@@ -499,12 +535,17 @@ def ours(args, world, rank, local):
                           "step_frac_of_peak": head_flops(C2_TOKENS, c2["n_labelled"])
                           / (c2["ms_per_step"] / 1000) / 1e12 / pk["bf16_tflops"],
                           "kernels_ms_per_step": {k: v[0] / args.steps for k, v in k2.items()
-                                                  if v[1]}}
+                                                  if v[1]},
+                          "host_ms_per_step": c2["host_ms_per_step"],
+                          "graph_ms_per_step": c2["graph_ms_per_step"]}
         nf4 = run_nf4(world, rank, args.steps, args.warmup, args.nf4_layers)
         if "c1" in nf4:
-            nf4["c1"]["roofline"] = {"bound": "hbm", "achieved": nf4["c1"]["kernel_GB_per_s"],
+            # average launch duration over the timed region (back-to-back launches between two
+            # events); the per-launch event pairs of the profile pass add their own overhead
+            # to a ~22 us kernel and are reported beside it as kernel_GB_per_s
+            nf4["c1"]["roofline"] = {"bound": "hbm", "achieved": nf4["c1"]["GB_per_s"],
                                      "peak": pk["hbm_gbs"], "unit": "GB/s",
-                                     "frac": nf4["c1"]["kernel_GB_per_s"] / pk["hbm_gbs"],
+                                     "frac": nf4["c1"]["GB_per_s"] / pk["hbm_gbs"],
                                      "traffic": profile_traffic("nf4_c1_layer")}
         nf4["c3"]["frac_of_hbm_per_gpu"] = nf4["c3"]["GB_per_s"] / world / pk["hbm_gbs"]
         line["nf4"] = nf4

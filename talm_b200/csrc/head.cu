@@ -198,6 +198,7 @@ __global__ void __launch_bounds__(LOGITS_THREADS, 1)
     if (p.n_grad > 0) prefetch_tmap(&tm_probs);
   }
   pair_setup(ctl, warp);
+  grid_dependency_wait();  // the previous kernel's outputs (statistics, probabilities, acc)
   const uint32_t tmem_base = ctl->tmem_base;
   volatile int* abort = &ctl->abort;
   const int n_tiles = p.n_pair_rows * p.n_col_tiles;
@@ -427,6 +428,7 @@ __global__ void __launch_bounds__(256) head_combine_kernel(const float4* __restr
                                                            __half* __restrict__ probs,
                                                            int probs_ld,
                                                            float* __restrict__ acc, int hidden) {
+  grid_dependency_wait();  // the slice's part statistics and probabilities
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
   if (row >= n_tokens) return;
@@ -588,6 +590,7 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
     prefetch_tmap(&tm_acc);
   }
   pair_setup(ctl, warp);
+  grid_dependency_wait();  // the previous kernel's outputs (statistics, probabilities, acc)
   const uint32_t tmem_base = ctl->tmem_base;
   volatile int* abort = &ctl->abort;
   const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
@@ -1045,13 +1048,16 @@ int launch_pair_kernel(void (*kernel)(CUtensorMap, CUtensorMap, CUtensorMap, Par
   cfg.blockDim = dim3(threads, 1, 1);
   cfg.dynamicSmemBytes = SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // the launch (and the set-up up to grid_dependency_wait) overlaps the previous kernel
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, m0, m1, m2, params);
   if (e != cudaSuccess) return set_error(TALM_ECUDA, "pair kernel launch: %s", cudaGetErrorString(e));
   return TALM_OK;
@@ -1181,12 +1187,24 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
       return check_launch("wait for the previous accumulator GEMM");
     {
       LaunchTimer timer(TALM_KERNEL_HEAD_COMBINE, stream);
-      head_combine_kernel<<<static_cast<int>((n_tokens + 7) / 8), 256, 0, stream>>>(
-          ws.partial, n_col_tiles * PARTS, static_cast<int>(n_tokens), static_cast<int>(n_grad), k == 0,
-          stats, n_grad > 0 ? ws.probs[buf] : nullptr, static_cast<int>(chunk),
-          n_grad > 0 ? acc : nullptr, static_cast<int>(hidden_size));
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>((n_tokens + 7) / 8), 1, 1);
+      cfg.blockDim = dim3(256, 1, 1);
+      cfg.stream = stream;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      const cudaError_t e = cudaLaunchKernelEx(
+          &cfg, head_combine_kernel, static_cast<const float4*>(ws.partial),
+          static_cast<int>(n_col_tiles * PARTS), static_cast<int>(n_tokens),
+          static_cast<int>(n_grad), static_cast<int>(k == 0), stats,
+          n_grad > 0 ? ws.probs[buf] : static_cast<__half*>(nullptr), static_cast<int>(chunk),
+          n_grad > 0 ? acc : static_cast<float*>(nullptr), static_cast<int>(hidden_size));
+      if (e != cudaSuccess)
+        return set_error(TALM_ECUDA, "head combine launch: %s", cudaGetErrorString(e));
     }
-    if ((st = check_launch("head combine kernel")) != TALM_OK) return st;
 
     if (n_grad > 0) {
       cudaStream_t acc_stream = pipe ? pipe->stream : stream;
