@@ -51,7 +51,8 @@ constexpr int TMEM_COLS = 2 * BN;           // double-buffered fp32 accumulator 
 // epilogue group used in turn, through which the epilogue's outputs leave by TMA store /
 // reduce-add instead of per-lane global stores; a group fills one buffer while the store of
 // the other is still reading it.
-constexpr int STAGING_BYTES = 4 * 16384;
+constexpr int STAGING_PER_GROUP = 2;  // staging buffers per epilogue group, used in turn
+constexpr int STAGING_BYTES = 2 * STAGING_PER_GROUP * 16384;
 constexpr int SMEM_BYTES =
     STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align slack*/ + 512 /*barriers*/;
 // Two epilogue groups of 4 warps (one warp per TMEM lane quarter in each group); group g owns
@@ -259,7 +260,7 @@ __global__ void __launch_bounds__(LOGITS_THREADS, 1)
     const int bar_id = 1 + g;
     const int r_in_tile = q * 32 + lane;
     const bool elected = (warp - 2) % 4 == 0 && lane == 0;  // the group's TMA-issuing thread
-    uint8_t* const bufs = staging + g * 2 * 16384;  // the group's two staging buffers
+    uint8_t* const bufs = staging + g * STAGING_PER_GROUP * 16384;  // the group's buffers
     int nb = 0;                                     // the one to fill next
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -350,9 +351,9 @@ __global__ void __launch_bounds__(LOGITS_THREADS, 1)
           if (store_p) {
             // the store issued from this buffer two blocks ago has read it (at most the last
             // store, from the other buffer, may still be reading)
-            if (elected) bulk_wait_read<1>();
+            if (elected) bulk_wait_read<STAGING_PER_GROUP - 1>();
             named_barrier(bar_id, EPI_THREADS);
-            nb ^= 1;
+            nb = (nb + 1) % STAGING_PER_GROUP;
           }
           chunk(full, 2 * kb, track, true, mscaled, store_p ? buf : nullptr, 0);
           chunk(full, 2 * kb + 1, track, true, mscaled, store_p ? buf : nullptr, 4);
@@ -658,7 +659,7 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
     const int bar_id = 1 + g;
     const int r_in_tile = q * 32 + lane;
     const bool elected = (warp - 2) % 4 == 0 && lane == 0;  // the group's TMA-issuing thread
-    uint8_t* const bufs = staging + g * 2 * 16384;  // the group's two staging buffers
+    uint8_t* const bufs = staging + g * STAGING_PER_GROUP * 16384;  // the group's buffers
     int nb = 0;                                     // the one to fill next
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -681,9 +682,9 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
         tmem_wait_ld();
         if (any_rows && ht * BN + c * 32 < p.hidden) {
           uint8_t* buf = bufs + nb * 16384;
-          nb ^= 1;
+          nb = (nb + 1) % STAGING_PER_GROUP;
           // the reduce issued from this buffer two chunks ago has read it
-          if (elected) bulk_wait_read<1>();
+          if (elected) bulk_wait_read<STAGING_PER_GROUP - 1>();
           named_barrier(bar_id, EPI_THREADS);
 #pragma unroll
           for (int v = 0; v < 8; ++v)
