@@ -18,7 +18,7 @@ Same line, secondary objects:
   e2e  the headline through the same API with host buffers: pinned-host -> device copies of the
        step's hidden states and labels and the device -> host read of the loss inside the timed
        region
-  roofline     the dominant kernel (head_logits_kernel) against the measured bf16/fp16 peak
+  roofline     the dominant kernel (head_slice_kernel) against the measured bf16/fp16 peak
   cpu_baseline the CPU oracle (a restatement of the reference's torch formula,
                solution/test_kernels.py:70-83) on a bounded sample, rank 0, N=1
 
@@ -472,15 +472,15 @@ def ours(args, world, rank, local):
 
     kernels = head["kernels"]
     total_ms = sum(v[0] for v in kernels.values()) or 1.0
-    lg_ms, lg_n = kernels["head_logits"]
+    # head_slice_kernel runs every tensor-core FLOP of the step: the logits GEMM of every row
+    # and the accumulator GEMM of the labelled rows over this rank's columns; one launch per
+    # slice step. achieved = algorithmic FLOPs per launch / average launch duration.
+    sl_ms, sl_n = kernels["head_slice"]
     cols_rank = weight.shape[0]
-    # algorithmic FLOPs of one logits launch: 2 H x (slice columns) x N; slices of CHUNK
-    n_slices = -(-cols_rank // CHUNK)
-    logits_flops = 2 * HIDDEN * cols_rank * n_tok / n_slices
-    ach = logits_flops / (lg_ms / max(lg_n, 1) / 1000) / 1e12 if lg_n else None
-    acc_ms, acc_n = kernels["head_accum"]
-    acc_flops = 2 * HIDDEN * cols_rank * n_lab / n_slices
-    acc_ach = acc_flops / (acc_ms / max(acc_n, 1) / 1000) / 1e12 if acc_n else None
+    step_flops = 2 * HIDDEN * cols_rank * (n_tok + n_lab)
+    launches_per_step = sl_n / max(args.steps, 1)
+    flops_per_launch = step_flops / launches_per_step if sl_n else None
+    ach = step_flops / (sl_ms / max(args.steps, 1) / 1000) / 1e12 if sl_n else None
     peak = pk["bf16_tflops_sustained"]
     line = {
         "metric": METRIC,
@@ -501,14 +501,13 @@ def ours(args, world, rank, local):
                    "global_batch": n_tok, "seq_len": n_tok, "hidden": HIDDEN, "vocab": VOCAB,
                    "parallelism": f"vocab{world}",
                    "l2": "inputs larger than L2 (weight 467 MB), no flush"},
-        "roofline": {"bound": "tensor", "kernel": "head_logits_kernel",
+        "roofline": {"bound": "tensor", "kernel": "head_slice_kernel",
                      "achieved": ach, "peak": peak, "unit": "TFLOP/s",
                      "frac": (ach / peak) if ach else None,
                      "peak_source": f"{pk['source']} bf16 sustained (kernel inside a long step)",
                      "frac_of_burst": (ach / pk["bf16_tflops"]) if ach else None,
-                     "traffic": profile_traffic("head_logits_c4"),
-                     "flops_per_launch": logits_flops,
-                     "accum_kernel_TFLOPs": acc_ach,
+                     "traffic": profile_traffic("head_slice_c4"),
+                     "flops_per_launch": flops_per_launch,
                      "step_TFLOPs": head_flops(n_tok, n_lab) / (head["ms_per_step"] / 1000)
                      / 1e12},
         "e2e": {"value": n_tok / (e2e_ms / 1000), "unit": "tokens/s",

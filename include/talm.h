@@ -53,9 +53,10 @@ int talm_device_status(int* status_out);
  * on those events and returns, per kernel kind, the summed device milliseconds and the launch
  * count (arrays of n_kinds entries, n_kinds <= TALM_KERNEL_KINDS). Off by default; when off the
  * launches carry no events. Not thread-safe: profile from one host thread. */
-#define TALM_KERNEL_HEAD_LOGITS 0   /* head_logits_kernel   (tcgen05 logits GEMM + stats) */
+#define TALM_KERNEL_HEAD_SLICE 0    /* head_slice_kernel (tcgen05 logits GEMM of a slice + stats,
+                                       with the accumulator GEMM of the slice before)    */
 #define TALM_KERNEL_HEAD_COMBINE 1  /* head_combine_kernel  (per-slice merge)             */
-#define TALM_KERNEL_HEAD_ACCUM 2    /* head_accum_kernel    (tcgen05 accumulator GEMM)    */
+#define TALM_KERNEL_HEAD_RESERVED 2 /* unused (the accumulator GEMM is part of HEAD_SLICE) */
 #define TALM_KERNEL_HEAD_FINALIZE 3 /* head_finalize_kernel                               */
 #define TALM_KERNEL_HEAD_MERGE 4    /* head_merge_shards_kernel                           */
 #define TALM_KERNEL_NF4 5           /* nf4 bulk-copy and chunk kernels (main body)        */

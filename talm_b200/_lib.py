@@ -98,7 +98,7 @@ def stream_of(device):
     return torch.cuda.current_stream(device).cuda_stream
 
 
-KERNEL_KINDS = ("head_logits", "head_combine", "head_accum", "head_finalize", "head_merge",
+KERNEL_KINDS = ("head_slice", "head_combine", "head_reserved", "head_finalize", "head_merge",
                 "nf4", "nf4_tail", "head_scale", "peer_publish", "peer_reduce", "peer_finish")
 
 

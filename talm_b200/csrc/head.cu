@@ -1,28 +1,30 @@
 // Fused LM head + cross-entropy, forward and backward, without materialised logits.
 //
-// The vocabulary (or this rank's shard of it) is walked in slices of `vocab_chunk` columns. Per
-// slice three launches run back to back on the caller's stream:
+// The vocabulary (or this rank's shard of it) is walked in slices (a narrow first slice, then
+// equal slices of at most `vocab_chunk` columns). Two kinds of work run per slice:
 //
-//   1. head_logits_kernel  (tcgen05, TMA-fed, persistent): tiles of 128 token rows x 256 vocab
-//      columns of z = fp16(h . W^T), K = hidden. The fp32 accumulator lives in TMEM (two
-//      256-column buffers, so the epilogue of one tile overlaps the MMAs of the next). The
-//      epilogue (4 warps, one token row per thread) rounds each logit to fp16 as the
-//      reference's cuBLAS output does, and computes the tile's row statistics: max m_t, first
-//      argmax, s_t = sum exp(z - m_t), t_t = sum exp(z - m_t) z, the target logit. For the
-//      labelled rows it writes p = fp16(exp(z - m_t)) into the slice's probability buffer (the
-//      only [rows, chunk] buffer of the head; it stays in L2 at the configured sizes).
-//   2. head_combine_kernel: one warp per row merges the slice's tile statistics with the running
-//      statistics of the earlier slices (log-sum-exp merge). A row whose reference moved in this
-//      slice (every row on the first slice, afterwards only a row whose max outgrew REF + 8) has
-//      its probability row rescaled in place to p * exp(m_t - m_new), so that it equals
-//      fp16(exp(z - REF_new)), the reference's in-place softmax weights, and its acc row
-//      multiplied by alpha = exp(REF_old - REF_new) (the online-softmax rescale of
-//      solution/fused_head.py:170-177). Every other row's probabilities are already relative to
-//      its reference.
-//   3. head_accum_kernel (tcgen05, persistent): acc[256 rows, 256 hidden] += P W_slice,
-//      K = slice columns, by TMA reduce-add into an acc that starts at zero. P and W_slice go
-//      TMA -> MMA untouched (W read MN-major, hidden contiguous, straight from the weight rows).
-//      The last, partial wave of tiles is split along K over all CTA pairs.
+//   * the logits GEMM (tcgen05, TMA-fed, CTA pairs): tiles of 256 token rows x 256 vocab columns
+//     of z = fp16(h . W^T), K = hidden. The fp32 accumulator lives in TMEM (two 256-column
+//     buffers, so the epilogue of one tile overlaps the MMAs of the next). The epilogue (two
+//     groups of 4 warps, one token row per thread) rounds each logit to fp16 as the reference's
+//     cuBLAS output does, and computes per 128-column part: max m_t, first argmax,
+//     s_t = sum exp(z - base), t_t = sum exp(z - base) z, the target logit; for the labelled
+//     rows it stores p = fp16(exp(z - base)) into the slice's probability buffer (the only
+//     [rows, chunk] buffer of the head), base = the row's reference REF (the part's max on the
+//     first slice, or where the max outgrew REF + 8);
+//   * the accumulator GEMM (same tiles, K = slice columns): acc[256 rows, 256 hidden] +=
+//     P W_slice by TMA reduce-add into an acc that starts at zero, P and W_slice TMA -> MMA
+//     untouched (W read MN-major, hidden contiguous, straight from the weight rows).
+//
+// head_slice_kernel runs the logits GEMM of slice s together with the accumulator GEMM of
+// slice s - 1 in one persistent launch (one list of whole tiles per CTA pair, balanced in
+// K-blocks: the logits tiles fill what the accumulator tiles leave), then head_combine_kernel
+// merges slice s's part statistics
+// into the running ones (log-sum-exp merge). A row whose reference moved in slice s (every row
+// on the first slice, afterwards only a row whose max outgrew REF + 8) has its probability row
+// rescaled in place to fp16(exp(z - REF_new)), the reference's in-place softmax weights, and its
+// acc row multiplied by alpha = exp(REF_old - REF_new) (the online-softmax rescale of
+// solution/fused_head.py:170-177) before the accumulator GEMM of slice s reads them.
 //
 // A last launch (head_finalize_kernel) turns the statistics into loss / entropy / correctness
 // and the accumulator into dH = acc / s - fp16(W[target]) (fused_head.py:111-125, :160-169),
@@ -64,14 +66,11 @@ constexpr int EPI_COLS = BN / EPI_GROUPS;      // 128 columns per group
 constexpr int EPI_WARPS = 4 * EPI_GROUPS;      // 8
 constexpr int EPI_THREADS = 128;               // threads per group
 constexpr int PARTS = EPI_GROUPS;              // statistics records per (row, tile)
-constexpr int LOGITS_THREADS = 32 * (2 + EPI_WARPS);       // producer, MMA, epilogue
-constexpr int ACCUM_THREADS = 32 * (2 + EPI_WARPS);       // producer, MMA, epilogue
+constexpr int SLICE_THREADS = 32 * (2 + EPI_WARPS);  // producer, MMA, epilogue warps
 constexpr float kLog2e = 1.4426950408889634f;
 // Slack of the lazy reference: a row's probabilities and accumulator stay relative to REF while
 // its running max is at most REF + kRefSlack, so p = exp(z - REF) <= e^8 (fits fp16).
 constexpr float kRefSlack = 8.0f;
-// Smallest K range (in BK blocks) of a split accumulator tile piece.
-constexpr int kMinSplitBlocks = 8;
 
 // M = 256 across the CTA pair, N = 256 (128 columns of B in each CTA's shared memory)
 constexpr uint32_t kIdescLogits = idesc_f16_f32(PAIR_ROWS, BN, false, false);  // A, B K-major
@@ -176,244 +175,6 @@ struct LogitsParams {
   float4* partial;    // [n_tokens][n_parts]: m, s, t, first argmax (int bits) per part
   float* stats;       // [n_tokens][TALM_HEAD_STATS]
 };
-
-// Pair tile t covers rows [pr * 256, +256) x columns [ct * 256, +256) of the slice; the CTA of
-// rank r owns rows pr * 256 + r * 128 + [0, 128) (its TMEM lanes) and loads B rows (weight
-// rows) ct * 256 + r * 128 + [0, 128); the pair's accumulator columns 0..127 come from the
-// leader's B half, 128..255 from the peer's.
-__global__ void __launch_bounds__(LOGITS_THREADS, 1)
-    head_logits_kernel(const __grid_constant__ CUtensorMap tm_hidden,
-                       const __grid_constant__ CUtensorMap tm_weight,
-                       const __grid_constant__ CUtensorMap tm_probs, LogitsParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = aligned_smem(smem_raw);
-  uint8_t* staging = smem + STAGES * STAGE_BYTES;
-  SharedCtl* ctl = reinterpret_cast<SharedCtl*>(staging + STAGING_BYTES);
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_ctarank();
-  const bool leader = rank == 0;
-  if (threadIdx.x == 0) {
-    prefetch_tmap(&tm_hidden);
-    prefetch_tmap(&tm_weight);
-    if (p.n_grad > 0) prefetch_tmap(&tm_probs);
-  }
-  pair_setup(ctl, warp);
-  grid_dependency_wait();  // the previous kernel's outputs (statistics, probabilities, acc)
-  const uint32_t tmem_base = ctl->tmem_base;
-  volatile int* abort = &ctl->abort;
-  const int n_tiles = p.n_pair_rows * p.n_col_tiles;
-  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
-
-  if (warp == 0) {
-    if (lane == 0) {  // TMA producer (both CTAs): this CTA's halves, counted on the leader
-      int stage = 0, issued = 0;
-      uint32_t phase = 0;
-      for (int tile = pair; tile < n_tiles && !*abort; tile += n_pairs) {
-        const int pr = tile % p.n_pair_rows, ct = tile / p.n_pair_rows;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort)) break;
-          uint8_t* a = smem + stage * STAGE_BYTES;
-          const uint32_t lfull = mapa_shared(smem_u32(&ctl->full[stage]), 0);
-          if (leader) mbar_arrive_expect_tx(&ctl->full[stage], 2 * STAGE_BYTES);
-          tma_load_2d_pair(a, &tm_hidden, lfull, kb * BK, pr * PAIR_ROWS + rank * BM);
-          tma_load_2d_pair(a + A_BYTES, &tm_weight, lfull, kb * BK,
-                           p.slice_row0 + ct * BN + rank * (BN / 2));
-          ++issued;
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
-        }
-      }
-      if (leader) drain_copies(ctl, stage, phase, issued);
-    }
-  } else if (warp == 1) {
-    if (lane == 0 && leader) {  // MMA issuer (leader only)
-      int stage = 0, acc = 0;
-      uint32_t phase = 0, acc_phase = 0;
-      for (int tile = pair; tile < n_tiles; tile += n_pairs) {
-        if (!mbar_wait(&ctl->tempty[acc], acc_phase ^ 1, abort)) break;
-        tc_fence_after();
-        const uint32_t d = tmem_base + acc * BN;
-        bool ok = true;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!mbar_wait(&ctl->full[stage], phase, abort)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t a = smem_u32(smem + stage * STAGE_BYTES);
-          const uint32_t b = a + A_BYTES;
-#pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            umma_f16_pair(d, smem_desc_sw128(a + k * 32, 16, 1024),
-                          smem_desc_sw128(b + k * 32, 16, 1024), kIdescLogits, (kb | k) != 0);
-          }
-          umma_commit_pair(&ctl->empty[stage]);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
-        }
-        if (!ok) break;
-        umma_commit_pair(&ctl->tfull[acc]);
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1;
-      }
-      drain_mmas(ctl);
-    }
-  } else {  // epilogue: warps 2..9 of both CTAs, TMEM lane quarter = warp % 4
-    const int q = warp & 3;
-    const int g = (warp - 2) >> 2;                    // epilogue group: columns g*128..+128
-    const int bar_id = 1 + g;
-    const int r_in_tile = q * 32 + lane;
-    const bool elected = (warp - 2) % 4 == 0 && lane == 0;  // the group's TMA-issuing thread
-    uint8_t* const bufs = staging + g * STAGING_PER_GROUP * 16384;  // the group's buffers
-    int nb = 0;                                     // the one to fill next
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    for (int tile = pair; tile < n_tiles; tile += n_pairs) {
-      const int pr = tile % p.n_pair_rows, ct = tile / p.n_pair_rows;
-      // CTA-uniform decision among the 4 epilogue warps (named barriers follow; every lane's
-      // wait is bounded, so every thread reaches the vote)
-      const bool landed = mbar_wait(&ctl->tfull[acc], acc_phase, abort);
-      if (named_barrier_or(bar_id, EPI_THREADS, !landed)) break;
-      tc_fence_after();
-      const int row0 = pr * PAIR_ROWS + rank * BM;  // first row of this CTA's half
-      const int row = row0 + r_in_tile;
-      const bool valid_row = row < p.n_tokens;
-      const long long tgt = valid_row ? p.targets[row] : -1;
-      const long long tile_col0 = p.col_base + static_cast<long long>(ct) * BN;
-      const long long tcol_ll = tgt - tile_col0;
-      const int tcol = (tgt >= 0 && tcol_ll >= g * EPI_COLS && tcol_ll < (g + 1) * EPI_COLS)
-                           ? static_cast<int>(tcol_ll) : -1;
-      const int ncols = min(BN, p.cols - ct * BN);  // valid columns of the tile (tile-relative)
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      // probabilities leave through the staging buffers by TMA store (64 columns = 16 KiB per
-      // store); CTAs whose rows are all unlabelled (or no gradient) skip them
-      const bool store_p = row0 < p.n_grad;
-
-      // Rows with a reference (every slice after the first) take ONE pass over TMEM: logits
-      // rounded to fp16, running max / first argmax / target logit, and s, t, p relative to
-      // REF. If some row's tile max outgrows REF + slack (its reference moves: rare), the CTA
-      // takes a second pass in which those rows use their tile max. The first slice (no
-      // reference yet) takes a max pass, then the sum pass relative to the tile max.
-      const float ref = (p.has_ref && valid_row)
-                            ? p.stats[static_cast<long long>(row) * TALM_HEAD_STATS + TALM_STAT_REF]
-                            : 0.0f;
-      const bool full_tile = ncols >= (g + 1) * EPI_COLS;  // the group's columns all valid
-      // is this warp's target column anywhere in the tile (then the per-element test runs)
-      const bool any_target = __any_sync(0xffffffffu, tcol >= 0);
-      float mx = -INFINITY, zt = 0.0f, s = 0.0f, t = 0.0f;
-      int arg = g * EPI_COLS;
-      uint32_t r[32];
-      // One 32-column chunk: `track` = max / argmax / target, `sum` = s, t and the
-      // probabilities (written to `buf`, 16-byte chunks qbase..qbase+3 of this row). The TMEM
-      // load is warp-collective (.sync.aligned): every lane executes it. `full` (a compile-time
-      // flag: the group's columns are all valid) drops the per-column bounds tests.
-      auto chunk = [&](auto full, int c, bool track, bool sum, float mscaled, uint8_t* buf,
-                       int qbase) {
-        constexpr bool kFull = decltype(full)::value;
-        tmem_ld_32x32b_x32(taddr + c * 32, r);
-        tmem_wait_ld();
-        uint32_t packed[16];
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const int col = c * 32 + j;
-          // fp16 rounding of the pair as the reference's fp16 GEMM output (one packed cvt)
-          const float2 z = __half22float2(
-              __floats2half2_rn(__uint_as_float(r[j]), __uint_as_float(r[j + 1])));
-          const bool ok0 = kFull || col < ncols;
-          const bool ok1 = kFull || col + 1 < ncols;
-          if (track) {
-            if (ok0 && z.x > mx) { mx = z.x; arg = col; }
-            if (ok1 && z.y > mx) { mx = z.y; arg = col + 1; }
-            if (any_target) {
-              if (col == tcol) zt = z.x;
-              if (col + 1 == tcol) zt = z.y;
-            }
-          }
-          if (sum) {
-            const float e0 = ok0 ? ex2(fmaf(z.x, kLog2e, -mscaled)) : 0.0f;
-            const float e1 = ok1 ? ex2(fmaf(z.y, kLog2e, -mscaled)) : 0.0f;
-            s += e0 + e1;
-            t = fmaf(e0, z.x, t);
-            t = fmaf(e1, z.y, t);
-            packed[j / 2] = pack_half2(e0, e1);
-          }
-        }
-        if (sum && buf != nullptr) {
-#pragma unroll
-          for (int v = 0; v < 4; ++v)
-            stage_chunk(buf, r_in_tile, qbase + v, packed[4 * v], packed[4 * v + 1],
-                        packed[4 * v + 2], packed[4 * v + 3]);
-        }
-      };
-      // A pass with sums over the group's columns: 2 blocks of 64 columns, each staged and
-      // stored. `base` per lane; `track` for the single-pass case.
-      auto sum_pass = [&](auto full, bool track, float base) {
-        const float mscaled = base * kLog2e;
-#pragma unroll 1
-        for (int kb = g * (EPI_COLS / 64); kb < (g + 1) * (EPI_COLS / 64); ++kb) {
-          uint8_t* buf = bufs + nb * 16384;
-          if (store_p) {
-            // the store issued from this buffer two blocks ago has read it (at most the last
-            // store, from the other buffer, may still be reading)
-            if (elected) bulk_wait_read<STAGING_PER_GROUP - 1>();
-            named_barrier(bar_id, EPI_THREADS);
-            nb = (nb + 1) % STAGING_PER_GROUP;
-          }
-          chunk(full, 2 * kb, track, true, mscaled, store_p ? buf : nullptr, 0);
-          chunk(full, 2 * kb + 1, track, true, mscaled, store_p ? buf : nullptr, 4);
-          if (store_p) {
-            fence_proxy_async_smem();
-            named_barrier(bar_id, EPI_THREADS);
-            if (elected) {
-              tma_store_2d(&tm_probs, buf, ct * BN + kb * 64, row0);
-              bulk_commit();
-            }
-          }
-        }
-      };
-      auto epilogue = [&](auto full) {
-        if (p.has_ref) {
-          s = 0.0f;
-          t = 0.0f;
-          sum_pass(full, true, ref);
-          const bool jump = mx > ref + kRefSlack;
-          if (named_barrier_or(bar_id, EPI_THREADS, jump)) {
-            // some row's reference moves in the group's columns: they are redone (rows
-            // without a move recompute the same values); earlier stores must land before the
-            // new ones
-            if (elected) bulk_wait_all();
-            named_barrier(bar_id, EPI_THREADS);
-            s = 0.0f;
-            t = 0.0f;
-            sum_pass(full, false, jump ? mx : ref);
-          }
-        } else {
-#pragma unroll 1
-          for (int c = g * (EPI_COLS / 32); c < (g + 1) * (EPI_COLS / 32); ++c)
-            chunk(full, c, true, false, 0.0f, nullptr, 0);
-          sum_pass(full, false, mx);
-        }
-      };
-      if (full_tile) {
-        epilogue(std::true_type{});
-      } else {
-        epilogue(std::false_type{});
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&ctl->tempty[acc]), 0));
-      if (valid_row) {
-        p.partial[static_cast<long long>(row) * p.n_parts + ct * PARTS + g] =
-            make_float4(mx, s, t, __int_as_float(static_cast<int>(tile_col0 + arg)));
-        if (tcol >= 0 && tcol < ncols) {
-          float* st = p.stats + static_cast<long long>(row) * TALM_HEAD_STATS;
-          st[TALM_STAT_ZT] = zt;
-          st[TALM_STAT_HIT] = 1.0f;
-        }
-      }
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1;
-    }
-    if (elected) bulk_wait_all();  // every probability store has landed before the CTA leaves
-  }
-  pair_teardown(ctl, warp, tmem_base);
-}
 
 // ------------------------------------------------------------------------------------------
 // 2. per-slice combine of tile statistics with the running statistics
@@ -534,49 +295,95 @@ struct AccumParams {
   int slice_row0;    // first weight row of the slice
   int n_pair_rows;   // ceil(n_grad / PAIR_ROWS)
   int n_h_tiles;     // ceil(hidden / BN)
-  int split;         // 1: the tiles of the last, partial wave are split along K over all pairs
 };
 
-// Work unit u of pair `pair`: K-blocks [kb0, kb1) of pair tile `tile`. Whole tiles go round-robin
-// over the pairs for as many full waves as the tile count allows; with `split`, the K-blocks of
-// the remaining tiles (fewer than one per pair) are cut into one contiguous range per pair, so
-// every pair ends at the same point ("stream-K" for the last wave). A range may span the end of
-// one tile and the start of the next: two units. Every unit's accumulator is added into acc by
-// TMA reduce-add, so the pieces of a split tile combine in any order.
-__device__ __forceinline__ bool accum_unit(const AccumParams& p, int pair, int n_pairs, int u,
-                                           int& tile, int& kb0, int& kb1) {
-  const int n_tiles = p.n_pair_rows * p.n_h_tiles, K = p.k_blocks;
-  const int waves = p.split ? n_tiles / n_pairs : (n_tiles + n_pairs - 1) / n_pairs;
-  if (u < waves) {
-    tile = pair + u * n_pairs;
-    kb0 = 0;
-    kb1 = K;
-    return tile < n_tiles;
-  }
-  const int rest = n_tiles - waves * n_pairs;
-  if (!p.split || rest <= 0) return false;
-  // at least kMinSplitBlocks K-blocks per piece, so that the MMAs outweigh the piece's epilogue
-  const long long total = static_cast<long long>(rest) * K;
-  const long long by_size = total / kMinSplitBlocks;
-  const int n_split = by_size < 1 ? 1 : (by_size < n_pairs ? static_cast<int>(by_size) : n_pairs);
-  if (pair >= n_split) return false;
-  const long long g0 = total * pair / n_split, g1 = total * (pair + 1) / n_split;
-  const long long t = g0 / K + (u - waves);
-  const long long b = max(g0, t * K), e = min(g1, (t + 1) * K);
-  if (b >= e) return false;
-  tile = waves * n_pairs + static_cast<int>(t);
-  kb0 = static_cast<int>(b - t * K);
-  kb1 = static_cast<int>(e - t * K);
-  return true;
+// ------------------------------------------------------------------------------------------
+// One launch per slice step: the logits GEMM of slice s and the accumulator GEMM of slice s - 1
+// share one persistent grid of CTA pairs, so that the accumulator work fills the logits GEMM's
+// last, partial wave (and vice versa) and a slice costs two launches (this and the combine).
+// ------------------------------------------------------------------------------------------
+struct SliceParams {
+  LogitsParams lg;  // logits GEMM of slice s: n_tiles_l pair tiles (0: none, the last step)
+  AccumParams ac;   // accumulator GEMM of slice s - 1: n_tiles_a pair tiles (0: none)
+  int n_tiles_l;
+  int n_tiles_a;
+};
+
+// A unit of work: a whole logits tile (type 0) or accumulator tile (type 1), K-blocks
+// [kb0, kb1).
+struct Unit {
+  int type, tile, kb0, kb1;
+};
+
+// This pair's share of a step, in whole tiles (so that every acc element receives exactly one
+// addition per slice: the sums are the same bits on every run). Accumulator tiles go
+// round-robin over the pairs; when their count is not a multiple of the pair count, the
+// first nA pairs hold one more accumulator tile than the other nB pairs, so the logits tiles
+// first go round-robin over those nB pairs (d each, d = K_a / K_l rounded: one accumulator
+// tile's worth of K-blocks), then round-robin over all pairs. Tiles that run at the same time
+// on different pairs stay neighbours in the tile order (the same weight columns, consecutive
+// row blocks), which keeps their operands shared in L2. Every role of both CTAs computes the
+// same plan and walks the same unit sequence: the accumulator tiles, then the logits tiles.
+struct PairPlan {
+  int n_a;      // accumulator tiles: pair + i * n_pairs
+  int n_l1;     // logits tiles of the first round-robin: (pair - nA) + i * nB
+  int n_l2;     // logits tiles of the second: base2 + pair + i * n_pairs
+  int nA, nB, base2;
+};
+
+__device__ __forceinline__ PairPlan plan_pair(const SliceParams& p, int pair, int n_pairs) {
+  const int ta = p.n_tiles_a, tl = p.n_tiles_l;
+  PairPlan r;
+  r.n_a = ta / n_pairs + (pair < ta % n_pairs ? 1 : 0);
+  r.nA = ta % n_pairs;
+  r.nB = n_pairs - r.nA;
+  int d = 0;
+  if (r.nA > 0 && tl > 0 && p.lg.k_blocks > 0)
+    d = min((p.ac.k_blocks + p.lg.k_blocks / 2) / p.lg.k_blocks, tl / r.nB);
+  r.n_l1 = pair >= r.nA ? d : 0;
+  r.base2 = d * r.nB;
+  r.n_l2 = tl - r.base2 > pair ? (tl - r.base2 - pair + n_pairs - 1) / n_pairs : 0;
+  return r;
 }
 
-// Pair tile t covers labelled rows [pr * 256, +256) x hidden columns [ht * 256, +256); the CTA
-// of rank r owns rows pr * 256 + r * 128 + [0, 128) and loads the hidden columns
+__device__ __forceinline__ bool slice_unit(const SliceParams& p, const PairPlan& plan, int pair,
+                                           int n_pairs, int u, Unit& out) {
+  out.kb0 = 0;
+  if (u < plan.n_a) {
+    out.type = 1;
+    out.tile = pair + u * n_pairs;
+    out.kb1 = p.ac.k_blocks;
+    return true;
+  }
+  u -= plan.n_a;
+  out.type = 0;
+  out.kb1 = p.lg.k_blocks;
+  if (u < plan.n_l1) {
+    out.tile = (pair - plan.nA) + u * plan.nB;
+    return true;
+  }
+  u -= plan.n_l1;
+  if (u < plan.n_l2) {
+    out.tile = plan.base2 + pair + u * n_pairs;
+    return true;
+  }
+  return false;
+}
+
+// Logits tile t covers rows [pr * 256, +256) x slice columns [ct * 256, +256) (pr = t % pair
+// rows); the CTA of rank r owns rows pr * 256 + r * 128 + [0, 128) (its TMEM lanes) and loads
+// weight rows ct * 256 + r * 128 + [0, 128) (K-major B): the pair's accumulator columns
+// 0..127 come from the leader's B half, 128..255 from the peer's. Accumulator tile t covers
+// labelled rows [pr * 256, +256) x hidden columns [ht * 256, +256) (ht = t % hidden tiles); the
+// CTA of rank r owns rows pr * 256 + r * 128 + [0, 128) and loads hidden columns
 // ht * 256 + r * 128 + [0, 128) of W (two 64-wide MN-major boxes per stage).
-__global__ void __launch_bounds__(ACCUM_THREADS, 1)
-    head_accum_kernel(const __grid_constant__ CUtensorMap tm_probs,
+__global__ void __launch_bounds__(SLICE_THREADS, 1)
+    head_slice_kernel(const __grid_constant__ CUtensorMap tm_hidden,
+                      const __grid_constant__ CUtensorMap tm_weight,
+                      const __grid_constant__ CUtensorMap tm_probs_out,
+                      const __grid_constant__ CUtensorMap tm_probs_in,
                       const __grid_constant__ CUtensorMap tm_weight_mn,
-                      const __grid_constant__ CUtensorMap tm_acc, AccumParams p) {
+                      const __grid_constant__ CUtensorMap tm_acc, SliceParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = aligned_smem(smem_raw);
   uint8_t* staging = smem + STAGES * STAGE_BYTES;
@@ -585,35 +392,51 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
+  const LogitsParams& lp = p.lg;
+  const AccumParams& ap = p.ac;
   if (threadIdx.x == 0) {
-    prefetch_tmap(&tm_probs);
-    prefetch_tmap(&tm_weight_mn);
-    prefetch_tmap(&tm_acc);
+    if (p.n_tiles_l > 0) {
+      prefetch_tmap(&tm_hidden);
+      prefetch_tmap(&tm_weight);
+      if (lp.n_grad > 0) prefetch_tmap(&tm_probs_out);
+    }
+    if (p.n_tiles_a > 0) {
+      prefetch_tmap(&tm_probs_in);
+      prefetch_tmap(&tm_weight_mn);
+      prefetch_tmap(&tm_acc);
+    }
   }
   pair_setup(ctl, warp);
   grid_dependency_wait();  // the previous kernel's outputs (statistics, probabilities, acc)
   const uint32_t tmem_base = ctl->tmem_base;
   volatile int* abort = &ctl->abort;
   const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+  const PairPlan plan = plan_pair(p, pair, n_pairs);
+  Unit unit;
 
   if (warp == 0) {
-    if (lane == 0) {  // TMA producer (both CTAs)
+    if (lane == 0) {  // TMA producer (both CTAs): this CTA's halves, counted on the leader
       int stage = 0, issued = 0;
       uint32_t phase = 0;
-      int tile, kb0, kb1;
-      for (int u = 0; !*abort && accum_unit(p, pair, n_pairs, u, tile, kb0, kb1); ++u) {
-        const int ht = tile % p.n_h_tiles, pr = tile / p.n_h_tiles;
-        for (int kb = kb0; kb < kb1; ++kb) {
+      for (int u = 0; !*abort && slice_unit(p, plan, pair, n_pairs, u, unit); ++u) {
+        for (int kb = unit.kb0; kb < unit.kb1; ++kb) {
           if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort)) break;
           uint8_t* a = smem + stage * STAGE_BYTES;
           const uint32_t lfull = mapa_shared(smem_u32(&ctl->full[stage]), 0);
-          const int row0 = pr * PAIR_ROWS + rank * BM;
           if (leader) mbar_arrive_expect_tx(&ctl->full[stage], 2 * STAGE_BYTES);
-          tma_load_2d_pair(a, &tm_probs, lfull, kb * BK, row0);
+          if (unit.type == 0) {
+            const int pr = unit.tile % lp.n_pair_rows, ct = unit.tile / lp.n_pair_rows;
+            tma_load_2d_pair(a, &tm_hidden, lfull, kb * BK, pr * PAIR_ROWS + rank * BM);
+            tma_load_2d_pair(a + A_BYTES, &tm_weight, lfull, kb * BK,
+                             lp.slice_row0 + ct * BN + rank * (BN / 2));
+          } else {
+            const int ht = unit.tile % ap.n_h_tiles, pr = unit.tile / ap.n_h_tiles;
+            tma_load_2d_pair(a, &tm_probs_in, lfull, kb * BK, pr * PAIR_ROWS + rank * BM);
 #pragma unroll
-          for (int j = 0; j < BN / 2 / 64; ++j)
-            tma_load_2d_pair(a + A_BYTES + j * (64 * BK * 2), &tm_weight_mn, lfull,
-                             ht * BN + rank * (BN / 2) + j * 64, p.slice_row0 + kb * BK);
+            for (int j = 0; j < BN / 2 / 64; ++j)
+              tma_load_2d_pair(a + A_BYTES + j * (64 * BK * 2), &tm_weight_mn, lfull,
+                               ht * BN + rank * (BN / 2) + j * 64, ap.slice_row0 + kb * BK);
+          }
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -624,24 +447,30 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
     if (lane == 0 && leader) {  // MMA issuer (leader only)
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
-      int tile, kb0, kb1;
-      for (int u = 0; accum_unit(p, pair, n_pairs, u, tile, kb0, kb1); ++u) {
+      for (int u = 0; slice_unit(p, plan, pair, n_pairs, u, unit); ++u) {
         if (!mbar_wait(&ctl->tempty[acc], acc_phase ^ 1, abort)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
         bool ok = true;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = unit.kb0; kb < unit.kb1; ++kb) {
           if (!mbar_wait(&ctl->full[stage], phase, abort)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a = smem_u32(smem + stage * STAGE_BYTES);
           const uint32_t b = a + A_BYTES;
+          if (unit.type == 0) {
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            // A: K-major rows of 128 B, +32 B per 16 K. B: MN-major, two 64-wide hidden groups
-            // of BK rows x 128 B (LBO = 8 KiB), 16 K-rows = +2 KiB.
-            umma_f16_pair(d, smem_desc_sw128(a + k * 32, 16, 1024),
-                          smem_desc_sw128(b + k * 2048, 64 * BK * 2, 1024), kIdescAccum,
-                          kb != kb0 || k != 0);
+            for (int k = 0; k < BK / 16; ++k)  // A and B K-major rows of 128 B, +32 B per 16 K
+              umma_f16_pair(d, smem_desc_sw128(a + k * 32, 16, 1024),
+                            smem_desc_sw128(b + k * 32, 16, 1024), kIdescLogits,
+                            kb != unit.kb0 || k != 0);
+          } else {
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              // A: K-major rows of 128 B, +32 B per 16 K. B: MN-major, two 64-wide hidden
+              // groups of BK rows x 128 B (LBO = 8 KiB), 16 K-rows = +2 KiB.
+              umma_f16_pair(d, smem_desc_sw128(a + k * 32, 16, 1024),
+                            smem_desc_sw128(b + k * 2048, 64 * BK * 2, 1024), kIdescAccum,
+                            kb != unit.kb0 || k != 0);
           }
           umma_commit_pair(&ctl->empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -653,9 +482,9 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
       }
       drain_mmas(ctl);
     }
-  } else {  // epilogue: warps 2..9 of both CTAs
+  } else {  // epilogue: warps 2..9 of both CTAs, TMEM lane quarter = warp % 4
     const int q = warp & 3;
-    const int g = (warp - 2) >> 2;                    // epilogue group: hidden columns g*128..
+    const int g = (warp - 2) >> 2;                    // epilogue group: columns g*128..+128
     const int bar_id = 1 + g;
     const int r_in_tile = q * 32 + lane;
     const bool elected = (warp - 2) % 4 == 0 && lane == 0;  // the group's TMA-issuing thread
@@ -663,47 +492,187 @@ __global__ void __launch_bounds__(ACCUM_THREADS, 1)
     int nb = 0;                                     // the one to fill next
     int acc = 0;
     uint32_t acc_phase = 0;
-    int tile, kb0, kb1;
-    for (int u = 0; accum_unit(p, pair, n_pairs, u, tile, kb0, kb1); ++u) {
-      const int ht = tile % p.n_h_tiles, pr = tile / p.n_h_tiles;
-      // CTA-uniform decision among the 4 epilogue warps (named barriers follow)
+    for (int u = 0; slice_unit(p, plan, pair, n_pairs, u, unit); ++u) {
+      // CTA-uniform decision among the 4 epilogue warps (named barriers follow; every lane's
+      // wait is bounded, so every thread reaches the vote)
       const bool landed = mbar_wait(&ctl->tfull[acc], acc_phase, abort);
       if (named_barrier_or(bar_id, EPI_THREADS, !landed)) break;
       tc_fence_after();
-      const int row0 = pr * PAIR_ROWS + static_cast<int>(rank) * BM;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      // acc += D by TMA reduce-add (acc starts at zero; a moved reference was applied to acc
-      // by the combine kernel before this launch)
-      const bool any_rows = row0 < p.n_grad;
-#pragma unroll 1
-      for (int c = g * (EPI_COLS / 32); c < (g + 1) * (EPI_COLS / 32); ++c) {
+      if (unit.type == 0) {  // logits tile: statistics and probabilities
+        const int pr = unit.tile % lp.n_pair_rows, ct = unit.tile / lp.n_pair_rows;
+        const int row0 = pr * PAIR_ROWS + rank * BM;  // first row of this CTA's half
+        const int row = row0 + r_in_tile;
+        const bool valid_row = row < lp.n_tokens;
+        const long long tgt = valid_row ? lp.targets[row] : -1;
+        const long long tile_col0 = lp.col_base + static_cast<long long>(ct) * BN;
+        const long long tcol_ll = tgt - tile_col0;
+        const int tcol = (tgt >= 0 && tcol_ll >= g * EPI_COLS && tcol_ll < (g + 1) * EPI_COLS)
+                             ? static_cast<int>(tcol_ll) : -1;
+        const int ncols = min(BN, lp.cols - ct * BN);  // valid columns of the tile (tile-relative)
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+        // probabilities leave through the staging buffers by TMA store (64 columns = 16 KiB per
+        // store); CTAs whose rows are all unlabelled (or no gradient) skip them
+        const bool store_p = row0 < lp.n_grad;
+
+        // Rows with a reference (every slice after the first) take ONE pass over TMEM: logits
+        // rounded to fp16, running max / first argmax / target logit, and s, t, p relative to
+        // REF. If some row's tile max outgrows REF + slack (its reference moves: rare), the CTA
+        // takes a second pass in which those rows use their tile max. The first slice (no
+        // reference yet) takes a max pass, then the sum pass relative to the tile max.
+        const float ref = (lp.has_ref && valid_row)
+                              ? lp.stats[static_cast<long long>(row) * TALM_HEAD_STATS + TALM_STAT_REF]
+                              : 0.0f;
+        const bool full_tile = ncols >= (g + 1) * EPI_COLS;  // the group's columns all valid
+        // is this warp's target column anywhere in the tile (then the per-element test runs)
+        const bool any_target = __any_sync(0xffffffffu, tcol >= 0);
+        float mx = -INFINITY, zt = 0.0f, s = 0.0f, t = 0.0f;
+        int arg = g * EPI_COLS;
         uint32_t r[32];
-        tmem_ld_32x32b_x32(taddr + c * 32, r);
-        tmem_wait_ld();
-        if (any_rows && ht * BN + c * 32 < p.hidden) {
-          uint8_t* buf = bufs + nb * 16384;
-          nb = (nb + 1) % STAGING_PER_GROUP;
-          // the reduce issued from this buffer two chunks ago has read it
-          if (elected) bulk_wait_read<STAGING_PER_GROUP - 1>();
-          named_barrier(bar_id, EPI_THREADS);
-#pragma unroll
-          for (int v = 0; v < 8; ++v)
-            stage_chunk(buf, r_in_tile, v, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
-          fence_proxy_async_smem();
-          named_barrier(bar_id, EPI_THREADS);
-          if (elected) {
-            tma_reduce_add_2d(&tm_acc, buf, ht * BN + c * 32, row0);
-            bulk_commit();
+        // One 32-column chunk: `track` = max / argmax / target, `sum` = s, t and the
+        // probabilities (written to `buf`, 16-byte chunks qbase..qbase+3 of this row). The TMEM
+        // load is warp-collective (.sync.aligned): every lane executes it. `full` (a compile-time
+        // flag: the group's columns are all valid) drops the per-column bounds tests.
+        auto chunk = [&](auto full, int c, bool track, bool sum, float mscaled, uint8_t* buf,
+                         int qbase) {
+          constexpr bool kFull = decltype(full)::value;
+          tmem_ld_32x32b_x32(taddr + c * 32, r);
+          tmem_wait_ld();
+          uint32_t packed[16];
+  #pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const int col = c * 32 + j;
+            // fp16 rounding of the pair as the reference's fp16 GEMM output (one packed cvt)
+            const float2 z = __half22float2(
+                __floats2half2_rn(__uint_as_float(r[j]), __uint_as_float(r[j + 1])));
+            const bool ok0 = kFull || col < ncols;
+            const bool ok1 = kFull || col + 1 < ncols;
+            if (track) {
+              if (ok0 && z.x > mx) { mx = z.x; arg = col; }
+              if (ok1 && z.y > mx) { mx = z.y; arg = col + 1; }
+              if (any_target) {
+                if (col == tcol) zt = z.x;
+                if (col + 1 == tcol) zt = z.y;
+              }
+            }
+            if (sum) {
+              const float e0 = ok0 ? ex2(fmaf(z.x, kLog2e, -mscaled)) : 0.0f;
+              const float e1 = ok1 ? ex2(fmaf(z.y, kLog2e, -mscaled)) : 0.0f;
+              s += e0 + e1;
+              t = fmaf(e0, z.x, t);
+              t = fmaf(e1, z.y, t);
+              packed[j / 2] = pack_half2(e0, e1);
+            }
+          }
+          if (sum && buf != nullptr) {
+  #pragma unroll
+            for (int v = 0; v < 4; ++v)
+              stage_chunk(buf, r_in_tile, qbase + v, packed[4 * v], packed[4 * v + 1],
+                          packed[4 * v + 2], packed[4 * v + 3]);
+          }
+        };
+        // A pass with sums over the group's columns: 2 blocks of 64 columns, each staged and
+        // stored. `base` per lane; `track` for the single-pass case.
+        auto sum_pass = [&](auto full, bool track, float base) {
+          const float mscaled = base * kLog2e;
+  #pragma unroll 1
+          for (int kb = g * (EPI_COLS / 64); kb < (g + 1) * (EPI_COLS / 64); ++kb) {
+            uint8_t* buf = bufs + nb * 16384;
+            if (store_p) {
+              // the store issued from this buffer two blocks ago has read it (at most the last
+              // store, from the other buffer, may still be reading)
+              if (elected) bulk_wait_read<STAGING_PER_GROUP - 1>();
+              named_barrier(bar_id, EPI_THREADS);
+              nb = (nb + 1) % STAGING_PER_GROUP;
+            }
+            chunk(full, 2 * kb, track, true, mscaled, store_p ? buf : nullptr, 0);
+            chunk(full, 2 * kb + 1, track, true, mscaled, store_p ? buf : nullptr, 4);
+            if (store_p) {
+              fence_proxy_async_smem();
+              named_barrier(bar_id, EPI_THREADS);
+              if (elected) {
+                tma_store_2d(&tm_probs_out, buf, ct * BN + kb * 64, row0);
+                bulk_commit();
+              }
+            }
+          }
+        };
+        auto epilogue = [&](auto full) {
+          if (lp.has_ref) {
+            s = 0.0f;
+            t = 0.0f;
+            sum_pass(full, true, ref);
+            const bool jump = mx > ref + kRefSlack;
+            if (named_barrier_or(bar_id, EPI_THREADS, jump)) {
+              // some row's reference moves in the group's columns: they are redone (rows
+              // without a move recompute the same values); earlier stores must land before the
+              // new ones
+              if (elected) bulk_wait_all();
+              named_barrier(bar_id, EPI_THREADS);
+              s = 0.0f;
+              t = 0.0f;
+              sum_pass(full, false, jump ? mx : ref);
+            }
+          } else {
+  #pragma unroll 1
+            for (int c = g * (EPI_COLS / 32); c < (g + 1) * (EPI_COLS / 32); ++c)
+              chunk(full, c, true, false, 0.0f, nullptr, 0);
+            sum_pass(full, false, mx);
+          }
+        };
+        if (full_tile) {
+          epilogue(std::true_type{});
+        } else {
+          epilogue(std::false_type{});
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&ctl->tempty[acc]), 0));
+        if (valid_row) {
+          lp.partial[static_cast<long long>(row) * lp.n_parts + ct * PARTS + g] =
+              make_float4(mx, s, t, __int_as_float(static_cast<int>(tile_col0 + arg)));
+          if (tcol >= 0 && tcol < ncols) {
+            float* st = lp.stats + static_cast<long long>(row) * TALM_HEAD_STATS;
+            st[TALM_STAT_ZT] = zt;
+            st[TALM_STAT_HIT] = 1.0f;
           }
         }
+      } else {  // accumulator K range: acc += D
+        const int ht = unit.tile % ap.n_h_tiles, pr = unit.tile / ap.n_h_tiles;
+        const int row0 = pr * PAIR_ROWS + static_cast<int>(rank) * BM;
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+        // acc += D by TMA reduce-add (acc starts at zero; a moved reference was applied to acc
+        // by the combine kernel before this launch)
+        const bool any_rows = row0 < ap.n_grad;
+  #pragma unroll 1
+        for (int c = g * (EPI_COLS / 32); c < (g + 1) * (EPI_COLS / 32); ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, r);
+          tmem_wait_ld();
+          if (any_rows && ht * BN + c * 32 < ap.hidden) {
+            uint8_t* buf = bufs + nb * 16384;
+            nb = (nb + 1) % STAGING_PER_GROUP;
+            // the reduce issued from this buffer two chunks ago has read it
+            if (elected) bulk_wait_read<STAGING_PER_GROUP - 1>();
+            named_barrier(bar_id, EPI_THREADS);
+  #pragma unroll
+            for (int v = 0; v < 8; ++v)
+              stage_chunk(buf, r_in_tile, v, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+            fence_proxy_async_smem();
+            named_barrier(bar_id, EPI_THREADS);
+            if (elected) {
+              tma_reduce_add_2d(&tm_acc, buf, ht * BN + c * 32, row0);
+              bulk_commit();
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&ctl->tempty[acc]), 0));
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&ctl->tempty[acc]), 0));
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
-    if (elected) bulk_wait_all();  // every accumulator update has landed before the CTA leaves
+    if (elected) bulk_wait_all();  // every store and reduce has landed before the CTA leaves
   }
   pair_teardown(ctl, warp, tmem_base);
 }
@@ -988,65 +957,31 @@ Workspace layout(int64_t n_tokens, int64_t n_grad, int64_t vocab_cols, int64_t v
   return w;
 }
 
-// The accumulator GEMM runs on a library-owned stream per device, forked from and joined back
-// into the caller's stream with events, so that it overlaps the next slice's logits GEMM. The
-// stream and its events are created once per device; calls from several host threads serialise
-// their enqueueing on a mutex (the GPU work of the calls then orders on the side stream).
-struct SidePipe {
-  cudaStream_t stream = nullptr;
-  cudaEvent_t combined[2] = {nullptr, nullptr};  // slice k's statistics ready (caller's stream)
-  cudaEvent_t drained[2] = {nullptr, nullptr};   // slice k's accumulator GEMM done (side stream)
-  bool ready = false;
-};
-constexpr int kMaxPipeDevices = 64;
-SidePipe g_pipes[kMaxPipeDevices];
-std::mutex g_pipe_mutex;
-
-int side_pipe(SidePipe** out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxPipeDevices)
-    return set_error(TALM_ENODEV, "no usable current device");
-  SidePipe& p = g_pipes[dev];
-  if (!p.ready) {
-    cudaError_t e = cudaStreamCreateWithFlags(&p.stream, cudaStreamNonBlocking);
-    for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
-      e = cudaEventCreateWithFlags(&p.combined[i], cudaEventDisableTiming);
-      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p.drained[i], cudaEventDisableTiming);
-    }
-    if (e != cudaSuccess)
-      return set_error(TALM_ECUDA, "side stream set-up: %s", cudaGetErrorString(e));
-    p.ready = true;
-  }
-  *out = &p;
-  return TALM_OK;
-}
-
+std::mutex g_attr_mutex;
 bool g_attrs_set = false;
 
 int set_attrs() {
+  std::lock_guard<std::mutex> lock(g_attr_mutex);
   if (g_attrs_set) return TALM_OK;
-  cudaError_t e = cudaFuncSetAttribute(head_logits_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(head_accum_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             SMEM_BYTES);
+  const cudaError_t e = cudaFuncSetAttribute(
+      head_slice_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   if (e != cudaSuccess) return set_error(TALM_ECUDA, "smem attribute: %s", cudaGetErrorString(e));
   g_attrs_set = true;
   return TALM_OK;
 }
 
-// Launch one of the pair GEMMs: clusters of 2 CTAs, one pair per 2 SMs at most, never more
-// pairs than tiles.
-template <class Params>
-int launch_pair_kernel(void (*kernel)(CUtensorMap, CUtensorMap, CUtensorMap, Params),
-                       int threads, int n_tiles, const CUtensorMap& m0, const CUtensorMap& m1,
-                       const CUtensorMap& m2, const Params& params, cudaStream_t stream,
-                       int max_pairs) {
-  int pairs = n_tiles < max_pairs ? n_tiles : max_pairs;
-  if (pairs < 1) pairs = 1;
+// Launch one slice step: clusters of 2 CTAs, at most one pair per 2 SMs, with programmatic
+// dependent launch (the launch and the kernel's set-up overlap the previous kernel).
+int launch_slice_step(const CUtensorMap& tm_hidden, const CUtensorMap& tm_weight,
+                      const CUtensorMap& tm_probs_out, const CUtensorMap& tm_probs_in,
+                      const CUtensorMap& tm_weight_mn, const CUtensorMap& tm_acc,
+                      const SliceParams& sp, cudaStream_t stream, int max_pairs) {
+  // one pair per tile at most
+  const long long want = static_cast<long long>(sp.n_tiles_l) + sp.n_tiles_a;
+  const int pairs = static_cast<int>(std::max(1LL, std::min<long long>(want, max_pairs)));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.blockDim = dim3(SLICE_THREADS, 1, 1);
   cfg.dynamicSmemBytes = SMEM_BYTES;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -1054,13 +989,13 @@ int launch_pair_kernel(void (*kernel)(CUtensorMap, CUtensorMap, CUtensorMap, Par
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  // the launch (and the set-up up to grid_dependency_wait) overlaps the previous kernel
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, m0, m1, m2, params);
-  if (e != cudaSuccess) return set_error(TALM_ECUDA, "pair kernel launch: %s", cudaGetErrorString(e));
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, head_slice_kernel, tm_hidden, tm_weight,
+                                           tm_probs_out, tm_probs_in, tm_weight_mn, tm_acc, sp);
+  if (e != cudaSuccess) return set_error(TALM_ECUDA, "slice kernel launch: %s", cudaGetErrorString(e));
   return TALM_OK;
 }
 
@@ -1126,15 +1061,6 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
 
   const Slices sl = slices_of(vocab_cols, chunk);
   const int64_t n_slices = sl.count;
-  std::lock_guard<std::mutex> lock(g_pipe_mutex);
-  // The accumulator GEMM goes to the side stream (overlapping the next slice's logits GEMM)
-  // only when it has fewer tiles than the GPU has SMs; a GEMM that fills the GPU on its own
-  // gains nothing from sharing it and runs in order on the caller's stream.
-  const int64_t grad_pairs =
-      ((n_grad + PAIR_ROWS - 1) / PAIR_ROWS) * ((hidden_size + BN - 1) / BN);
-  SidePipe* pipe = nullptr;
-  if (n_grad > 0 && n_slices > 1 && grad_pairs < sms / 2 && (st = side_pipe(&pipe)) != TALM_OK)
-    return st;
 
   if (cudaMemsetAsync(stats, 0, sizeof(float) * TALM_HEAD_STATS * n_tokens, stream) != cudaSuccess)
     return check_launch("stats memset");
@@ -1146,46 +1072,55 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
   const int k_blocks = static_cast<int>((hidden_size + BK - 1) / BK);
   const int n_pair_rows = static_cast<int>((n_tokens + PAIR_ROWS - 1) / PAIR_ROWS);
   const int max_pairs = max_pairs_of(sms);
-  for (int64_t k = 0; k < n_slices; ++k) {
-    const int64_t s0 = sl.begin(k);
+  // Step k runs the logits GEMM of slice k (k < n_slices) together with the accumulator GEMM
+  // of slice k - 1 (k >= 1), then the combine of slice k. The slices' probability buffers
+  // alternate: step k writes buffer k % 2 while its accumulator part reads buffer (k - 1) % 2.
+  // The combine of slice k follows the accumulator GEMM of slice k - 1 (its acc rescale needs
+  // that) and precedes the one of slice k (which reads the rows it rescales).
+  AccumParams prev_ap{};
+  CUtensorMap prev_tm_probs = tm_hidden;
+  for (int64_t k = 0; k <= n_slices; ++k) {
+    SliceParams sp{};
+    sp.n_tiles_l = 0;
+    sp.n_tiles_a = 0;
+    CUtensorMap tm_probs_out = tm_hidden;  // unused when no probabilities are stored
+    int n_col_tiles = 0;
     const int buf = static_cast<int>(k & 1);
-    const int64_t s1 = std::min<int64_t>(vocab_cols, k == 0 ? sl.first : s0 + sl.width);
-    const int cols = static_cast<int>(s1 - s0);
-    const int n_col_tiles = (cols + BN - 1) / BN;
-    // the pair of buffers this slice writes is free once slice k - 2's accumulator GEMM is done
-    if (pipe && k >= 2 && cudaStreamWaitEvent(stream, pipe->drained[buf], 0) != cudaSuccess)
-      return check_launch("wait for slice buffers");
-    LogitsParams lp;
-    lp.n_tokens = static_cast<int>(n_tokens);
-    lp.n_grad = static_cast<int>(n_grad);
-    lp.k_blocks = k_blocks;
-    lp.slice_row0 = static_cast<int>(s0);
-    lp.cols = cols;
-    lp.n_col_tiles = n_col_tiles;
-    lp.n_parts = n_col_tiles * PARTS;
-    lp.n_pair_rows = n_pair_rows;
-    lp.col_base = vocab_col0 + s0;
-    lp.has_ref = k != 0;
-    lp.targets = reinterpret_cast<const long long*>(targets);
-    lp.partial = ws.partial;
-    lp.stats = stats;
-    CUtensorMap tm_probs = tm_hidden;  // unused when no probabilities are stored
-    if (n_grad > 0 &&
-        (st = talm_make_tmap_2d_f16(&tm_probs, ws.probs[buf], chunk, n_grad, chunk, 64, BM)) !=
-            TALM_OK)
-      return st;
-    {
-      LaunchTimer timer(TALM_KERNEL_HEAD_LOGITS, stream);
-      st = launch_pair_kernel(head_logits_kernel, LOGITS_THREADS, n_pair_rows * n_col_tiles, tm_hidden,
-                              tm_weight, tm_probs, lp, stream, max_pairs);
+    const int64_t s0 = k < n_slices ? sl.begin(k) : 0;
+    if (k < n_slices) {
+      const int64_t s1 = std::min<int64_t>(vocab_cols, k == 0 ? sl.first : s0 + sl.width);
+      const int cols = static_cast<int>(s1 - s0);
+      n_col_tiles = (cols + BN - 1) / BN;
+      LogitsParams& lp = sp.lg;
+      lp.n_tokens = static_cast<int>(n_tokens);
+      lp.n_grad = static_cast<int>(n_grad);
+      lp.k_blocks = k_blocks;
+      lp.slice_row0 = static_cast<int>(s0);
+      lp.cols = cols;
+      lp.n_col_tiles = n_col_tiles;
+      lp.n_parts = n_col_tiles * PARTS;
+      lp.n_pair_rows = n_pair_rows;
+      lp.col_base = vocab_col0 + s0;
+      lp.has_ref = k != 0;
+      lp.targets = reinterpret_cast<const long long*>(targets);
+      lp.partial = ws.partial;
+      lp.stats = stats;
+      sp.n_tiles_l = n_pair_rows * n_col_tiles;
+      if (n_grad > 0 && (st = talm_make_tmap_2d_f16(&tm_probs_out, ws.probs[buf], chunk, n_grad,
+                                                    chunk, 64, BM)) != TALM_OK)
+        return st;
     }
-    if (st != TALM_OK) return st;
-    // the combine rescales acc rows whose reference moved: the previous slice's accumulator
-    // GEMM (on the side stream) must have finished. (The probability rows it rescales are this
-    // slice's, in the buffer the logits GEMM just wrote.)
-    if (pipe && k >= 1 &&
-        cudaStreamWaitEvent(stream, pipe->drained[(k - 1) & 1], 0) != cudaSuccess)
-      return check_launch("wait for the previous accumulator GEMM");
+    if (k >= 1 && n_grad > 0) {
+      sp.ac = prev_ap;
+      sp.n_tiles_a = prev_ap.n_pair_rows * prev_ap.n_h_tiles;
+    }
+    if (sp.n_tiles_l + sp.n_tiles_a > 0) {
+      LaunchTimer timer(TALM_KERNEL_HEAD_SLICE, stream);
+      st = launch_slice_step(tm_hidden, tm_weight, tm_probs_out, prev_tm_probs, tm_weight_mn,
+                             tm_acc, sp, stream, max_pairs);
+      if (st != TALM_OK) return st;
+    }
+    if (k == n_slices) break;
     {
       LaunchTimer timer(TALM_KERNEL_HEAD_COMBINE, stream);
       cudaLaunchConfig_t cfg = {};
@@ -1206,35 +1141,15 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
       if (e != cudaSuccess)
         return set_error(TALM_ECUDA, "head combine launch: %s", cudaGetErrorString(e));
     }
-
-    if (n_grad > 0) {
-      cudaStream_t acc_stream = pipe ? pipe->stream : stream;
-      if (pipe && (cudaEventRecord(pipe->combined[buf], stream) != cudaSuccess ||
-                   cudaStreamWaitEvent(pipe->stream, pipe->combined[buf], 0) != cudaSuccess))
-        return check_launch("fork to the side stream");
-
-      AccumParams ap;
-      ap.n_grad = static_cast<int>(n_grad);
-      ap.hidden = static_cast<int>(hidden_size);
-      ap.k_blocks = n_col_tiles * (BN / BK);
-      ap.slice_row0 = static_cast<int>(s0);
-      ap.n_pair_rows = static_cast<int>((n_grad + PAIR_ROWS - 1) / PAIR_ROWS);
-      ap.n_h_tiles = static_cast<int>((hidden_size + BN - 1) / BN);
-      // a GEMM that runs alone on the caller's stream splits its last wave over all pairs
-      ap.split = pipe ? 0 : 1;
-      {
-        LaunchTimer timer(TALM_KERNEL_HEAD_ACCUM, acc_stream);
-        st = launch_pair_kernel(head_accum_kernel, ACCUM_THREADS, ap.n_pair_rows * ap.n_h_tiles, tm_probs,
-                                tm_weight_mn, tm_acc, ap, acc_stream, max_pairs);
-      }
-      if (st != TALM_OK) return st;
-      if (pipe && cudaEventRecord(pipe->drained[buf], pipe->stream) != cudaSuccess)
-        return check_launch("side stream event");
-    }
+    // the accumulator GEMM of this slice runs in the next step
+    prev_ap.n_grad = static_cast<int>(n_grad);
+    prev_ap.hidden = static_cast<int>(hidden_size);
+    prev_ap.k_blocks = n_col_tiles * (BN / BK);
+    prev_ap.slice_row0 = static_cast<int>(s0);
+    prev_ap.n_pair_rows = static_cast<int>((n_grad + PAIR_ROWS - 1) / PAIR_ROWS);
+    prev_ap.n_h_tiles = static_cast<int>((hidden_size + BN - 1) / BN);
+    prev_tm_probs = tm_probs_out;
   }
-  // join: the caller's stream continues after the last accumulator GEMM
-  if (pipe && cudaStreamWaitEvent(stream, pipe->drained[(n_slices - 1) & 1], 0) != cudaSuccess)
-    return check_launch("join the side stream");
   return TALM_OK;
 }
 
