@@ -81,7 +81,6 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-__device__ __forceinline__ float round_f16(float v) { return __half2float(__float2half_rn(v)); }
 
 // Barriers of a CTA of a pair. The pair leader (cluster rank 0) issues every MMA; `full` and
 // `tempty` are waited on in the leader only and receive arrivals / transaction bytes from both
@@ -896,8 +895,8 @@ __global__ void __launch_bounds__(256) head_merge_shards_kernel(const float* gat
 // ------------------------------------------------------------------------------------------
 // host side
 // ------------------------------------------------------------------------------------------
-// Slice buffers come in pairs: the accumulator GEMM of slice k (side stream) reads pair k % 2
-// while the logits GEMM and the combine of slice k + 1 (caller's stream) write the other one.
+// Probability buffers come in pairs: the slice step that runs the accumulator GEMM of slice k
+// reads buffer k % 2 while its logits GEMM of slice k + 1 writes the other one.
 struct Workspace {
   __half* probs[2];      // [n_grad][chunk] each
   float4* partial;       // [n_tokens][chunk / EPI_COLS]
