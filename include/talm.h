@@ -194,6 +194,19 @@ int talm_head_finalize(const float* stats, const int64_t* targets, int64_t n_tok
 int talm_head_combine(const float* gathered, int64_t n_shards, int64_t n_tokens, int64_t rank,
                       int64_t n_grad, float* stats_out, float* acc_scale, void* stream);
 
+/* The labelled-first row order (solution/fused_head.py:290-299 labelled_first) on the device,
+ * and the rows gathered in that order. targets: [n_tokens] int64 (-100 = unlabelled);
+ * n_labelled: the exact count of targets >= 0 (a wrong count leaves rows unwritten and records
+ * TALM_ERANGE in talm_device_status). src[i] = input row at position i (labelled rows first,
+ * each group in input order); dest (optional, NULL to skip) its inverse. With hidden_out
+ * (NULL to skip): hidden_out[i] = hidden[src[i]] ([n_tokens, cols] fp16, contiguous; rows of
+ * 16-byte multiples on 16-byte boundaries) and targets_out[i] = targets[src[i]]. Replaces the
+ * labelled_first call and the two index_select of FusedHeadLossVocab.forward (:326-336). */
+int talm_head_labelled_first(const int64_t* targets, int64_t n_tokens, int64_t n_labelled,
+                             const uint16_t* hidden, int64_t ld_hidden, int64_t cols,
+                             int64_t* src, int64_t* dest, uint16_t* hidden_out,
+                             int64_t* targets_out, void* stream);
+
 /* The head's backward: out = out_dtype(float(fp16(grad)) * s), s = grad_loss / denom, or 0
  * when denom == 0 (grad_loss, denom: fp32 scalars in device memory). grad is [n_rows, n_cols]
  * with a row stride of ld_grad elements, fp16 (grad_is_f32 == 0) or fp32 (grad_is_f32 != 0:

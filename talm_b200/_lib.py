@@ -38,6 +38,7 @@ SIGNATURES = {
                                   _P, _P, _P, _P, _INT, _P]),
     "talm_head_combine": (_INT, [_P, _I64, _I64, _I64, _I64, _P, _P, _P]),
     "talm_head_scale_grad": (_INT, [_P, _I64, _INT, _P, _P, _I64, _I64, _P, _INT, _P]),
+    "talm_head_labelled_first": (_INT, [_P, _I64, _I64, _P, _I64, _I64, _P, _P, _P, _P, _P]),
     "talm_peer_buffer_size": (_INT, [_I64, _I64, _I64, ctypes.POINTER(_SZ)]),
     "talm_ipc_export": (_INT, [_P, _P, ctypes.POINTER(_I64)]),
     "talm_ipc_import": (_INT, [_P, _I64, ctypes.POINTER(_P)]),

@@ -784,6 +784,76 @@ __global__ void __launch_bounds__(256) head_finalize_kernel(
 }
 
 // ------------------------------------------------------------------------------------------
+// labelled-first row order on the device (solution/fused_head.py:290-299)
+// ------------------------------------------------------------------------------------------
+// One CTA scans the labelled flags (target >= 0) 1024 rows at a time: with c(r) the labelled
+// rows among 0..r, dest[r] = c(r) - 1 for a labelled row and r - c(r) + n_labelled for an
+// unlabelled one (labelled rows first, each group in input order), src[dest[r]] = r. A
+// dest outside [0, n) (n_labelled not the true count) is not written and records TALM_ERANGE.
+__global__ void __launch_bounds__(1024) head_order_kernel(const long long* __restrict__ targets,
+                                                          int n, int n_labelled,
+                                                          long long* __restrict__ src,
+                                                          long long* __restrict__ dest) {
+  __shared__ int warp_sums[32];
+  __shared__ int carry;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < n; base += 1024) {
+    const int r = base + static_cast<int>(threadIdx.x);
+    const int f = (r < n && targets[r] >= 0) ? 1 : 0;
+    int x = f;  // inclusive count within the warp
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int w = warp_sums[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      warp_sums[lane] = w;  // inclusive over the warps
+    }
+    __syncthreads();
+    const int incl = carry + x + (warp > 0 ? warp_sums[warp - 1] : 0);
+    if (r < n) {
+      const long long d = f ? incl - 1 : static_cast<long long>(r) - incl + n_labelled;
+      if (d >= 0 && d < n) {
+        if (dest != nullptr) dest[r] = d;
+        src[d] = r;
+      } else {
+        atomicCAS(&g_device_status, 0, TALM_ERANGE);
+      }
+    }
+    __syncthreads();  // every thread has read `carry` and `warp_sums`
+    if (threadIdx.x == 1023) carry = incl;
+    __syncthreads();
+  }
+}
+
+// Rows in src order: out[i] = in[src[i]] (16-byte pieces), targets_out[i] = targets[src[i]].
+__global__ void __launch_bounds__(256) head_gather_rows_kernel(
+    const uint4* __restrict__ in, long long ld16, int n, int row16,
+    const long long* __restrict__ src, const long long* __restrict__ targets,
+    uint4* __restrict__ out, long long* __restrict__ targets_out) {
+  const long long total = static_cast<long long>(n) * row16;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += stride) {
+    const long long row = i / row16;
+    const int c = static_cast<int>(i - row * row16);
+    const long long from = src[row];
+    out[i] = in[from * ld16 + c];
+    if (c == 0) targets_out[row] = targets[from];
+  }
+}
+
+// ------------------------------------------------------------------------------------------
 // 5. backward: the saved gradient times grad_loss / denom, in the hidden's dtype
 // ------------------------------------------------------------------------------------------
 template <int OUT>
@@ -1256,6 +1326,45 @@ int talm_head_scale_grad(const void* grad, int64_t ld_grad, int grad_is_f32,
 #undef TALM_SCALE_BY_INPUT
 #undef TALM_SCALE_LAUNCH
   return check_launch("head scale kernel");
+}
+
+int talm_head_labelled_first(const int64_t* targets, int64_t n_tokens, int64_t n_labelled,
+                             const uint16_t* hidden, int64_t ld_hidden, int64_t cols,
+                             int64_t* src, int64_t* dest, uint16_t* hidden_out,
+                             int64_t* targets_out, void* stream) {
+  using namespace talm;
+  if (n_tokens < 0 || n_labelled < 0 || n_labelled > n_tokens)
+    return set_error(TALM_EINVAL, "need 0 <= n_labelled <= n_tokens");
+  if (n_tokens >= (int64_t{1} << 31)) return set_error(TALM_ERANGE, "n_tokens beyond 2^31");
+  if (n_tokens == 0) return TALM_OK;
+  if (!targets || !src) return set_error(TALM_EINVAL, "null pointer");
+  const bool rows = hidden_out != nullptr;
+  if (rows) {
+    if (!hidden || !targets_out) return set_error(TALM_EINVAL, "null pointer");
+    if (cols < 8 || cols % 8 != 0 || ld_hidden % 8 != 0 || ld_hidden < cols ||
+        (reinterpret_cast<uintptr_t>(hidden) & 15) != 0 ||
+        (reinterpret_cast<uintptr_t>(hidden_out) & 15) != 0)
+      return set_error(TALM_EINVAL, "hidden rows must be 16-byte aligned multiples of 8 columns");
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  head::head_order_kernel<<<1, 1024, 0, s>>>(reinterpret_cast<const long long*>(targets),
+                                             static_cast<int>(n_tokens),
+                                             static_cast<int>(n_labelled),
+                                             reinterpret_cast<long long*>(src),
+                                             reinterpret_cast<long long*>(dest));
+  int st = check_launch("head order kernel");
+  if (st != TALM_OK || !rows) return st;
+  const int row16 = static_cast<int>(cols / 8);
+  const long long items = n_tokens * row16;
+  const int sms = current_sm_count();
+  if (sms <= 0) return set_error(TALM_ENODEV, "no CUDA device");
+  const long long want = (items + 255) / 256;
+  const int grid = static_cast<int>(want < int64_t{sms} * 8 ? want : int64_t{sms} * 8);
+  head::head_gather_rows_kernel<<<grid, 256, 0, s>>>(
+      reinterpret_cast<const uint4*>(hidden), ld_hidden / 8, static_cast<int>(n_tokens), row16,
+      reinterpret_cast<const long long*>(src), reinterpret_cast<const long long*>(targets),
+      reinterpret_cast<uint4*>(hidden_out), reinterpret_cast<long long*>(targets_out));
+  return check_launch("head gather rows kernel");
 }
 
 int talm_head_combine(const float* gathered, int64_t n_shards, int64_t n_tokens, int64_t rank,

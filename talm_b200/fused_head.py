@@ -81,6 +81,25 @@ def labelled_first(labelled, n_labelled):
     return dest, src
 
 
+def labelled_first_rows(h16, targets, n_labelled):
+    """Device-side labelled-first compaction (talm_head_labelled_first): the fp16 rows and
+    their targets in the order of `labelled_first`, and `src` (the input row of each position),
+    in two launches instead of labelled_first + two index_select. h16: [N, cols] fp16 rows of
+    16-byte multiples on 16-byte boundaries; n_labelled: the exact count of targets >= 0.
+    (FusedHeadLossVocab keeps the reference's torch ops for this step: measured on config 2,
+    the device version did not make the step faster.)"""
+    lib = _lib.load()
+    n, cols = h16.shape
+    src = torch.empty(n, dtype=torch.int64, device=h16.device)
+    rows = torch.empty(n, cols, dtype=torch.float16, device=h16.device)
+    rows_targets = torch.empty(n, dtype=torch.int64, device=h16.device)
+    _lib.check(lib.talm_head_labelled_first(
+        _lib.ptr(targets), n, n_labelled, _lib.ptr(h16), h16.stride(0), cols, _lib.ptr(src), None,
+        _lib.ptr(rows), _lib.ptr(rows_targets), _lib.stream_of(h16.device)),
+        "talm_head_labelled_first")
+    return rows, rows_targets, src
+
+
 def _pad8(n):
     return (n + 7) // 8 * 8
 

@@ -112,3 +112,8 @@ def test_peer_exchange_and_backward_reject_bad_arguments(lib):
     assert lib.talm_head_scale_grad(None, 8, 0, None, None, 4, 8, None, 7, None) == 1
     assert lib.talm_head_scale_grad(None, 4, 0, None, None, 4, 8, None, 0, None) == 1
     assert lib.talm_head_scale_grad(None, 8, 0, None, None, 0, 8, None, 0, None) == 0
+
+
+def test_labelled_first_rejects_bad_arguments(lib):
+    assert lib.talm_head_labelled_first(None, 4, 5, None, 8, 8, None, None, None, None, None) == 1
+    assert lib.talm_head_labelled_first(None, 0, 0, None, 8, 8, None, None, None, None, None) == 0

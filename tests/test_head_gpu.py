@@ -304,3 +304,21 @@ def test_backward_scale_kernel_matches_oracle(out_dtype):
             ref = scale_grad(g, gl_t, ctx.denom, out_dtype)
             assert out.dtype == out_dtype and out.shape == g.shape
             assert torch.equal(out, ref), (tuple(g.shape), g.dtype, gl, dn)
+
+
+@pytest.mark.parametrize("n,frac", [(1, 0.5), (1000, 0.45), (1024, 0.0), (3001, 1.0), (20000, 0.3)])
+def test_device_labelled_first_matches_reference_order(n, frac):
+    """talm_head_labelled_first (one scanning CTA + a row gather) against labelled_first
+    (fused_head.py:290-299) and index_select: identical order, rows and targets."""
+    from talm_b200.fused_head import labelled_first, labelled_first_rows
+
+    g = torch.Generator(device=DEV).manual_seed(n)
+    targets = torch.randint(0, 1000, (n,), generator=g, device=DEV)
+    targets[torch.rand(n, generator=g, device=DEV) < frac] = -100
+    hidden = torch.randn(n, 40, generator=g, device=DEV).half()
+    n_lab = int((targets >= 0).sum())
+    rows, rows_targets, src = labelled_first_rows(hidden, targets, n_lab)
+    _dest, ref_src = labelled_first(targets >= 0, n_lab)
+    assert torch.equal(src, ref_src)
+    assert torch.equal(rows, hidden.index_select(0, ref_src))
+    assert torch.equal(rows_targets, targets.index_select(0, ref_src))
