@@ -12,10 +12,12 @@ reference's semantics (fused_head.py:53-58, :447-462):
 
 and the hidden gradient computed in the same forward (dH = softmax(z) W16 - W16[y]), saved for a
 backward that only scales it (fused_head.py:280-287). The whole vocabulary walk runs in
-libtalm_b200 (csrc/head.cu): per slice a tcgen05 logits GEMM with the statistics fused into
-its epilogue, a per-row merge, and a tcgen05 accumulator GEMM over the labelled rows. The host
-code here keeps the reference's contract around it: the labelled-first row order
-(`labelled_first`), the denominator, the autograd Function and the module switches.
+libtalm_b200 (csrc/head.cu) as one persistent tcgen05 launch per vocabulary slice -- the logits
+tiles of slice s, with the row statistics fused into their epilogue, together with the
+accumulator tiles (softmax(z) W over the labelled rows) of slice s-1 -- each followed by a
+per-row merge launch. The host code here keeps the reference's contract around it: the
+labelled-first row order (`labelled_first`; `labelled_first_rows` is the same order built on
+the device), the denominator, the autograd Function and the module switches.
 """
 
 import os
