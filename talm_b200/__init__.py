@@ -4,6 +4,7 @@ behind the reference's own Python entry points.
   fused_head      fused_head_loss / FusedHeadLossVocab / FusedHeadLoss / labelled_first
   qgroup          LayerGroup / GroupLinear / launch / patch_group_dequant
   nf4_dequant     nf4_dequantize / NF4_TABLE / patch_bnb_dequant
+  nf4_format      the stored 4-bit checkpoint format -> LayerGroup buffers / NF4Linear
   vocab_parallel  the head sharded by vocabulary over torch.distributed (NCCL)
 
 `apply()` installs the patches of these paths the way `solution.apply()` does

@@ -75,6 +75,20 @@ def _state_ok(state, first):
             and torch.equal(state.state2.code, first.state2.code))
 
 
+def _joined(parts):
+    """One flat tensor holding `parts` in order. Parts that already lie back to back in one
+    allocation (a loader wrote them there: nf4_format.load_layer) are adopted as one view of it;
+    anything else is concatenated into a new buffer."""
+    first = parts[0]
+    storage, offset = first.untyped_storage().data_ptr(), first.storage_offset()
+    for p in parts:
+        if (p.dtype != first.dtype or p.device != first.device or not p.is_contiguous()
+                or p.untyped_storage().data_ptr() != storage or p.storage_offset() != offset):
+            return torch.cat(parts)
+        offset += p.numel()
+    return first.as_strided((offset - first.storage_offset(),), (1,), first.storage_offset())
+
+
 class LayerGroup:
     """The seven 4-bit projections of one decoder layer, packed, with per-pass caches."""
 
@@ -109,9 +123,9 @@ class LayerGroup:
         self.row_bounds = [e // qblock for e in self.elem_bounds]
 
         # One buffer per array; each parameter / quant state becomes a view into it.
-        self.packed = torch.cat([m.weight.data.reshape(-1) for m in modules])
-        self.absmax8 = torch.cat([s.absmax.reshape(-1) for s in states])
-        self.absmax2 = torch.cat([s.state2.absmax.reshape(-1) for s in states])
+        self.packed = _joined([m.weight.data.reshape(-1) for m in modules])
+        self.absmax8 = _joined([s.absmax.reshape(-1) for s in states])
+        self.absmax2 = _joined([s.state2.absmax.reshape(-1) for s in states])
         byte = row = row2 = 0
         for m, s, n in zip(modules, states, numels):
             m.weight.data = self.packed[byte:byte + n // 2].view(-1, 1)
