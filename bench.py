@@ -21,6 +21,8 @@ Same line, secondary objects:
   roofline     the dominant kernel (head_slice_kernel) against the measured bf16/fp16 peak
   cpu_baseline the CPU oracle (a restatement of the reference's torch formula,
                solution/test_kernels.py:70-83) on a bounded sample, rank 0, N=1
+  c5   (--qlora, N=1) config 5: the full QLoRA step of the Qwen2.5-1.5B architecture with both
+       paths plugged in (talm_b200/qlora.py); `--only-qlora` prints it alone
 
 `--impl reference` times the reference's CPU formula (the oracle port) on the box's host cores
 on a bounded sample per step and prints the same metric with "impl": "reference"; under
@@ -68,6 +70,10 @@ def parse_args():
                    help="the NF4 part alone (profiling runs); prints its JSON object")
     p.add_argument("--nf4-layers", type=int, default=N_LAYERS,
                    help="layers in the config-3 sweep (fewer: a small case for ncu captures)")
+    p.add_argument("--qlora", action="store_true",
+                   help="add config 5 (the full QLoRA step, N=1) as the `c5` object")
+    p.add_argument("--only-qlora", action="store_true",
+                   help="config 5 alone; prints its JSON object")
     return p.parse_args()
 
 
@@ -255,6 +261,48 @@ def nf4_layer(seed, device, double_quant):
                                   device=device))
     return {"packed": packed, "absmax8": absmax8, "code": code, "absmax2": absmax2,
             "offset2": torch.cat(offsets), "out": out, "n": n}
+
+
+def run_qlora(steps, warmup, batch=4, seq=512):
+    """Config 5: one QLoRA training step of the Qwen2.5-1.5B architecture (random init, NF4 base
+    weights, LoRA r=16 alpha=32 on q_proj / v_proj) on a 4 x 512 batch with ~45% trailing pad,
+    both hot paths plugged in (talm_b200.qlora). Step = forward with labels + backward + AdamW
+    on the adapters; device time over `steps` steps after `warmup`."""
+    from talm_b200 import qlora
+
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    model = qlora.build_model(qlora.qwen25_15b_config(), "cuda", seed=0)
+    qlora.patch()
+    model.train()
+    opt = torch.optim.AdamW(qlora.adapters(model), lr=2e-4)
+    data = qlora.make_batch(batch, seq, VOCAB, "cuda", seed=0)
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    losses = []
+
+    def step():
+        losses.append(qlora.train_step(model, opt, data))
+
+    for _ in range(warmup):
+        step()
+    ms = timed(step, steps, 1, "qlora")
+    prof = profile_kernels(step, steps)
+    loss = [float(x) for x in losses]
+    n_tok = batch * seq
+    n_lab = int((data["labels"][:, 1:] >= 0).sum())
+    mem = torch.cuda.max_memory_allocated() / 2**30
+    del model, opt
+    torch.cuda.empty_cache()
+    return {"workload": "config 5: QLoRA step of Qwen2.5-1.5B (random init, NF4 double-quant "
+                        "base, LoRA r=16 alpha=32 on q/v), batch 4 x 512, ~45% trailing pad "
+                        "(padded batch with attention mask, not varlen-packed), fp16, 1 GPU",
+            "ms_per_step": ms / steps, "tokens_per_s": n_tok / (ms / steps / 1000),
+            "labelled_tokens": n_lab, "host_ms_per_step": HOST_MS.get("qlora"),
+            "build_s": build_s, "max_allocated_GiB": mem,
+            "loss_first_last": [loss[0], loss[-1]],
+            "kernels_ms_per_step": {k: v[0] / steps for k, v in prof.items() if v[1]},
+            "launches_per_step": {k: v[1] / steps for k, v in prof.items() if v[1]}}
 
 
 # ------------------------------------------------------------------------------------------
@@ -551,6 +599,10 @@ def ours(args, world, rank, local):
         if world == 1 and rank == 0:
             line["cpu_baseline"] = cpu_head_baseline(weight, c4_inputs("cuda")[0],
                                                      c4_inputs("cuda")[1])
+    if args.qlora and world == 1:
+        weight = weight_full = None
+        torch.cuda.empty_cache()
+        line["c5"] = run_qlora(args.steps, args.warmup)
     return line
 
 
@@ -600,6 +652,10 @@ def main():
     try:
         if args.only_nf4:
             line = {"nf4": run_nf4(world, rank, args.steps, args.warmup, args.nf4_layers)}
+        elif args.only_qlora:
+            if world != 1:
+                raise SystemExit("--only-qlora runs on one GPU")
+            line = {"c5": run_qlora(args.steps, args.warmup)}
         else:
             line = ours(args, world, rank, local)
         if rank == 0:

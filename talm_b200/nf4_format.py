@@ -218,6 +218,7 @@ def load_layer(source, prefix, device, projections=qgroup.PROJECTIONS):
     group = qgroup.LayerGroup(list(modules.values()))
     for idx, module in enumerate(modules.values()):
         module._talm_group = (group, idx)
+    qgroup.track(group)
     return group, modules
 
 

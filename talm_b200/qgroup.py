@@ -296,6 +296,11 @@ class GroupLinear(torch.autograd.Function):
 _GROUPS = []
 
 
+def track(group):
+    """Count `group` among the live layer groups that `reset_passes` resets."""
+    _GROUPS.append(weakref.ref(group))
+
+
 def reset_passes():
     """Reset every live layer group's pass state (qgroup.py:362-373)."""
     alive = []
@@ -308,8 +313,12 @@ def reset_passes():
 
 
 def _bnb_linear(module):
-    """The bitsandbytes Linear4bit under a PEFT wrapper (or the module itself)."""
-    import bitsandbytes as bnb
+    """The bitsandbytes Linear4bit under a PEFT wrapper (or the module itself); None for any
+    other module, and for every module when bitsandbytes is not installed."""
+    try:
+        import bitsandbytes as bnb
+    except ImportError:
+        return None
 
     base = getattr(module, "base_layer", module)
     return base if isinstance(base, bnb.nn.Linear4bit) else None
@@ -353,7 +362,7 @@ def _pack(layer):
         group.depth = n_layers - 1 - layer_idx
     for idx, base in enumerate(modules):
         base._talm_group = (group, idx)
-    _GROUPS.append(weakref.ref(group))
+    track(group)
     return group
 
 
@@ -392,11 +401,9 @@ def enter_layer(layer):
 prepare_layer = enter_layer
 
 
-def patch_group_dequant():
-    """`Qwen2DecoderLayer.forward` packs its layer on first use and starts its passes afresh;
-    `bitsandbytes.nn.Linear4bit.forward` routes packed modules through GroupLinear for fp16
-    CUDA inputs (qgroup.py:498-545)."""
-    import bitsandbytes as bnb
+def patch_decoder_layer():
+    """`Qwen2DecoderLayer.forward` packs its layer on first use and starts its passes afresh
+    (qgroup.py:474-492); installed once."""
     from transformers.models.qwen2 import modeling_qwen2
 
     layer_cls = modeling_qwen2.Qwen2DecoderLayer
@@ -412,6 +419,14 @@ def patch_group_dequant():
         forward._original = layer_forward
         layer_cls.forward = forward
 
+
+def patch_group_dequant():
+    """`Qwen2DecoderLayer.forward` packs its layer on first use and starts its passes afresh;
+    `bitsandbytes.nn.Linear4bit.forward` routes packed modules through GroupLinear for fp16
+    CUDA inputs (qgroup.py:498-545)."""
+    import bitsandbytes as bnb
+
+    patch_decoder_layer()
     lin_cls = bnb.nn.Linear4bit
     if getattr(lin_cls.forward, "_talm_group", False):
         return True

@@ -1,0 +1,227 @@
+"""A QLoRA training step of the Qwen2 architecture with both hot paths plugged in.
+
+`build_model(config, device)` makes transformers' `Qwen2ForCausalLM` in fp16 (random init),
+replaces the seven projections of every decoder layer by `NF4Linear` modules packed into one
+`LayerGroup` (read by `nf4_format.load_layer` from a seeded 4-bit checkpoint in the stored
+format) and wraps q_proj and v_proj in `LoraLinear` adapters. Only the adapters train. With
+`patch()` installed (the decoder-layer hook of `qgroup` and the fused head of `patches`), one
+`train_step` is: forward with labels (each layer's seven weights dequantised by one grouped
+launch per pass, the loss by the fused head with no logits tensor), backward (the head's saved
+dH scaled by one kernel, each layer dequantised once more), and one AdamW step on the adapters.
+The reference's step plugs the same two paths into the same model (solution/patches.py:173-260
+for the head call, solution/qgroup.py:474-545 for the layer hooks, solution/lora.py:151-231 for
+the adapter arithmetic).
+
+What the reference's step has that this one does not: PEFT and trl around the model, the varlen
+packing of the batch (solution/unpad.py; here the padded batch runs with an attention mask and
+the head skips the -100 rows), a gradient scaler for fp16 training (here the frozen model is
+fp16 and the adapters fp32, with no loss scaling), and gradient checkpointing.
+"""
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from . import nf4_format, qgroup
+
+LORA_TARGETS = ("self_attn.q_proj", "self_attn.v_proj")
+
+
+def qwen25_15b_config(**overrides):
+    """The Qwen2.5-1.5B architecture: 28 layers, hidden 1536, 12 query / 2 key-value heads of
+    128, SwiGLU 8960, tied vocabulary of 151936, RMSNorm eps 1e-6, RoPE theta 1e6."""
+    from transformers import Qwen2Config
+
+    args = dict(vocab_size=151936, hidden_size=1536, intermediate_size=8960,
+                num_hidden_layers=28, num_attention_heads=12, num_key_value_heads=2,
+                rms_norm_eps=1e-6, rope_theta=1e6, tie_word_embeddings=True,
+                max_position_embeddings=32768, attention_dropout=0.0)
+    args.update(overrides)
+    return Qwen2Config(**args)
+
+
+class LoraLinear(torch.nn.Module):
+    """base(x) + scaling * B(A(dropout(x))): the adapter of PEFT's 4-bit Linear under fp16
+    autocast, which the reference's LoraProjectionTorch reproduces op for op
+    (solution/lora.py:151-231): dropout of the input, the fp32 adapter weights cast to fp16, two
+    fp16 GEMMs ([T, in] x [in, r], then [T, r] x [r, out]), the product times scaling, added to
+    the base output. A is Kaiming-uniform and B zero at initialisation, as PEFT does; autograd
+    derives the backward."""
+
+    def __init__(self, base, r, alpha, dropout, generator=None, b_std=0.0):
+        super().__init__()
+        self.base = base
+        self.r, self.scaling, self.dropout = r, alpha / r, dropout
+        device = base.weight.device
+        a = torch.empty(r, base.in_features, dtype=torch.float32, device=device)
+        torch.nn.init.kaiming_uniform_(a, a=math.sqrt(5), generator=generator)
+        b = torch.zeros(base.out_features, r, dtype=torch.float32, device=device)
+        if b_std:
+            b.normal_(0.0, b_std, generator=generator)
+        self.lora_A = torch.nn.Parameter(a)
+        self.lora_B = torch.nn.Parameter(b)
+
+    @property
+    def in_features(self):
+        return self.base.in_features
+
+    @property
+    def out_features(self):
+        return self.base.out_features
+
+    def forward(self, x):
+        out = self.base(x)
+        xd = F.dropout(x, self.dropout, self.training) if self.dropout > 0 else x
+        t = torch.matmul(xd.to(torch.float16), self.lora_A.to(torch.float16).t())
+        branch = torch.matmul(t, self.lora_B.to(torch.float16).t())
+        return out + (branch * self.scaling).to(out.dtype)
+
+
+def projection_shapes(config):
+    """[out, in] of the seven projections of one decoder layer, in `qgroup.PROJECTIONS` order."""
+    hidden, inter = config.hidden_size, config.intermediate_size
+    head_dim = getattr(config, "head_dim", None) or hidden // config.num_attention_heads
+    q, kv = config.num_attention_heads * head_dim, config.num_key_value_heads * head_dim
+    shapes = [(q, hidden), (kv, hidden), (kv, hidden), (hidden, q), (inter, hidden),
+              (inter, hidden), (hidden, inter)]
+    return dict(zip(qgroup.PROJECTIONS, shapes))
+
+
+def code_table(generator, device):
+    """A seeded, sorted 256-entry code for the first-level scales, spanning [-1, 1] (the role of
+    bitsandbytes' dynamic map in a double-quantised checkpoint)."""
+    code = torch.sort(torch.rand(256, generator=generator, device=device) * 2 - 1).values
+    code[0], code[-1] = -1.0, 1.0
+    return code
+
+
+def synthetic_layer_checkpoint(shapes, prefix, generator, device, code, qblock=64, qblock2=256,
+                               scale=0.035, biases=None):
+    """A seeded 4-bit layer in the stored format (nf4_format): uniform codes and coded scales,
+    second-level scales in [0.2, 0.4] * scale and offset `scale`, so that every block scale is
+    code * absmax2 + offset in [0.6, 1.4] * scale (weights of standard deviation ~0.58 * scale:
+    ~0.02 at the default). `biases` maps a projection to an fp16 bias to store with it."""
+    sd = {}
+    levels = torch.tensor(qgroup.NF4_LEVELS, dtype=torch.float32, device=device)
+    for path, (o, i) in shapes.items():
+        n = o * i
+        n_blocks = n // qblock
+        w = f"{prefix}{path}.weight"
+        sd[w] = torch.randint(0, 256, (n // 2, 1), generator=generator, device=device,
+                              dtype=torch.uint8)
+        sd[w + ".absmax"] = torch.randint(0, 256, (n_blocks,), generator=generator,
+                                          device=device, dtype=torch.uint8)
+        sd[w + ".quant_map"] = levels.clone()
+        sd[w + ".nested_absmax"] = (torch.rand(-(-n_blocks // qblock2), generator=generator,
+                                               device=device) * 0.2 + 0.2) * scale
+        sd[w + ".nested_quant_map"] = code
+        sd[f"{w}.{nf4_format.QUANT_STATE_KEY}"] = nf4_format.pack_scalars(
+            {"quant_type": "nf4", "blocksize": qblock, "dtype": "float16", "shape": [o, i],
+             "nested_blocksize": qblock2, "nested_offset": float(scale),
+             "nested_dtype": "float32"})
+        if biases is not None and biases.get(path) is not None:
+            sd[f"{prefix}{path}.bias"] = biases[path]
+    return sd
+
+
+def _child(root, path):
+    obj = root
+    for part in path.split("."):
+        obj = getattr(obj, part)
+    return obj
+
+
+def _replace(root, path, module):
+    parent, _, name = path.rpartition(".")
+    setattr(_child(root, parent) if parent else root, name, module)
+
+
+def build_model(config, device, seed=0, lora_r=16, lora_alpha=32, lora_dropout=0.05,
+                lora_targets=LORA_TARGETS, qblock=64, qblock2=256, weight_scale=0.035,
+                lora_b_std=0.0):
+    """`Qwen2ForCausalLM(config)` in fp16 on `device` (random init from `seed`), its decoder
+    projections 4-bit (`NF4Linear`, one `LayerGroup` per layer, loaded from a synthetic stored
+    checkpoint) and LoRA on `lora_targets`; every parameter but the adapters frozen. The fp16
+    projection weights the constructor made are freed layer by layer before the 4-bit ones are
+    loaded. `lora_b_std` > 0 starts B at random instead of zero (tests use it to give A a
+    gradient on the first step)."""
+    from transformers import Qwen2ForCausalLM
+
+    device = torch.device(device)
+    torch.manual_seed(seed)
+    previous = torch.get_default_dtype()
+    torch.set_default_dtype(torch.float16)
+    try:
+        with device:
+            model = Qwen2ForCausalLM(config)
+    finally:
+        torch.set_default_dtype(previous)
+    generator = torch.Generator(device=device).manual_seed(seed + 1)
+    lora_generator = torch.Generator(device=device).manual_seed(seed + 2)
+    code = code_table(generator, device)
+    shapes = projection_shapes(config)
+    layers = model.model.layers
+    for index, layer in enumerate(layers):
+        prefix = f"model.layers.{index}."
+        biases = {}
+        for path in qgroup.PROJECTIONS:
+            bias = _child(layer, path).bias
+            biases[path] = None if bias is None else bias.detach().to(torch.float16)
+            _replace(layer, path, None)
+        sd = synthetic_layer_checkpoint(shapes, prefix, generator, device, code, qblock,
+                                        qblock2, weight_scale, biases)
+        group, modules = nf4_format.load_layer(sd, prefix, device)
+        del sd
+        group.depth = len(layers) - 1 - index
+        for path, module in modules.items():
+            if path in lora_targets:
+                module = LoraLinear(module, lora_r, lora_alpha, lora_dropout, lora_generator,
+                                    lora_b_std)
+            _replace(layer, path, module)
+        layer._talm_layer_group = group
+        layer._talm_group_done = True
+    for name, param in model.named_parameters():
+        param.requires_grad_(name.rsplit(".", 1)[-1] in ("lora_A", "lora_B"))
+    model.config.use_cache = False
+    return model
+
+
+def adapters(model):
+    """The trainable parameters (the LoRA A and B of every adapted projection)."""
+    return [p for p in model.parameters() if p.requires_grad]
+
+
+def patch():
+    """Install what the step runs through: the decoder-layer hook that starts each layer's
+    dequantisation passes, and the fused head in Qwen2ForCausalLM.forward."""
+    from .patches import patch_qwen2_causal_lm
+
+    qgroup.patch_decoder_layer()
+    patch_qwen2_causal_lm()
+
+
+def make_batch(batch, seq, vocab, device, seed=0, pad_fraction=0.45):
+    """Token ids uniform over the vocabulary, each row with a seeded trailing pad of 35-55 % of
+    the sequence, the last row's adjusted so the batch has ~`pad_fraction` pad (BASELINE config
+    5's batch shape); attention mask 0 and label -100 on the pad."""
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.randint(0, vocab, (batch, seq), generator=g)
+    lo, hi = int(0.35 * seq), int(0.55 * seq)
+    pads = torch.randint(lo, max(hi, lo + 1), (batch,), generator=g)
+    if batch > 1:
+        rest = int(round(pad_fraction * batch * seq)) - int(pads[:-1].sum())
+        pads[-1] = min(max(rest, 0), seq - 1)
+    keep = torch.arange(seq)[None, :] < (seq - pads)[:, None]
+    labels = ids.masked_fill(~keep, -100)
+    return {"input_ids": ids.to(device), "attention_mask": keep.to(torch.long).to(device),
+            "labels": labels.to(device)}
+
+
+def train_step(model, optimizer, batch):
+    """Forward with labels, backward, one optimizer step; returns the loss (a device scalar)."""
+    out = model(**batch)
+    out.loss.backward()
+    optimizer.step()
+    optimizer.zero_grad(set_to_none=True)
+    return out.loss.detach()
