@@ -288,9 +288,28 @@ def run_qlora(steps, warmup, batch=4, seq=512):
         step()
     ms = timed(step, steps, 1, "qlora")
     prof = profile_kernels(step, steps)
-    loss = [float(x) for x in losses]
     n_tok = batch * seq
-    n_lab = int((data["labels"][:, 1:] >= 0).sum())
+    n_lab = qlora.labelled_count(data["labels"])
+
+    # the same step with the decoder's forward and backward replayed as CUDA graphs
+    try:
+        gstep = qlora.GraphedStep(model, opt, data)
+
+        def graphed_step():
+            losses.append(gstep(data, n_lab))
+
+        for _ in range(warmup):
+            graphed_step()
+        gms = timed(graphed_step, steps, 1, "qlora_graphed")
+        gprof = profile_kernels(graphed_step, steps)
+        graphed = {"ms_per_step": gms / steps, "tokens_per_s": n_tok / (gms / steps / 1000),
+                   "host_ms_per_step": HOST_MS.get("qlora_graphed"),
+                   "eager_kernels_ms_per_step": {k: v[0] / steps for k, v in gprof.items()
+                                                 if v[1]}}
+        del gstep
+    except Exception as exc:  # noqa: BLE001 - reported in the line, the eager number stands
+        graphed = {"error": f"{type(exc).__name__}: {exc}"[:400]}
+    loss = [float(x) for x in losses]
     mem = torch.cuda.max_memory_allocated() / 2**30
     del model, opt
     torch.cuda.empty_cache()
@@ -302,7 +321,8 @@ def run_qlora(steps, warmup, batch=4, seq=512):
             "build_s": build_s, "max_allocated_GiB": mem,
             "loss_first_last": [loss[0], loss[-1]],
             "kernels_ms_per_step": {k: v[0] / steps for k, v in prof.items() if v[1]},
-            "launches_per_step": {k: v[1] / steps for k, v in prof.items() if v[1]}}
+            "launches_per_step": {k: v[1] / steps for k, v in prof.items() if v[1]},
+            "graphed": graphed}
 
 
 # ------------------------------------------------------------------------------------------

@@ -225,3 +225,65 @@ def train_step(model, optimizer, batch):
     optimizer.step()
     optimizer.zero_grad(set_to_none=True)
     return out.loss.detach()
+
+
+def causal_padding_mask(attention_mask):
+    """[B, 1, S, S] bool: query i of row b sees key j when j <= i and key j is not pad -- the
+    mask transformers builds from a right-padded [B, S] mask for SDPA, made here once so that
+    the decoder's forward reads no mask values on the host."""
+    seq = attention_mask.shape[1]
+    causal = torch.ones(seq, seq, dtype=torch.bool, device=attention_mask.device).tril()
+    return causal[None, None] & attention_mask.bool()[:, None, None, :]
+
+
+class _Decoder(torch.nn.Module):
+    """input ids + prepared 4-D mask -> last hidden state of the model's decoder."""
+
+    def __init__(self, model):
+        super().__init__()
+        self.decoder = model.model
+
+    def forward(self, input_ids, mask4d):
+        return self.decoder(input_ids=input_ids, attention_mask=mask4d,
+                            use_cache=False).last_hidden_state
+
+
+class GraphedStep:
+    """The training step with the decoder's forward and backward replayed as CUDA graphs.
+
+    The decoder (embedding, 28 layers, final norm) issues thousands of small launches per step
+    from Python; captured once for the batch shape (`torch.cuda.make_graphed_callables`), each
+    direction is one graph launch. Inside the graphs every layer still dequantises its seven
+    weights with one grouped launch per pass. The head stays eager: its row compaction depends
+    on the batch's labelled count (`n_labelled`, taken from the host batch, so no host sync),
+    and it is a handful of launches. The optimizer step runs eagerly after the backward.
+    Batches must keep the captured shape; the LayerGroups' pass bookkeeping runs during the
+    capture and the graphs replay its launches."""
+
+    def __init__(self, model, optimizer, batch, warmup=3):
+        self.model, self.optimizer = model, optimizer
+        ids, mask = batch["input_ids"], batch["attention_mask"]
+        self.shape = tuple(ids.shape)
+        self.decoder = torch.cuda.make_graphed_callables(
+            _Decoder(model), (ids.clone(), causal_padding_mask(mask)),
+            num_warmup_iters=warmup)
+
+    def __call__(self, batch, n_labelled):
+        ids, mask, labels = batch["input_ids"], batch["attention_mask"], batch["labels"]
+        if tuple(ids.shape) != self.shape:
+            raise ValueError(f"batch shape {tuple(ids.shape)} is not the captured {self.shape}")
+        from .fused_head import fused_head_loss
+
+        hidden = self.decoder(ids, causal_padding_mask(mask))
+        shift = F.pad(labels, (0, 1), value=-100)[:, 1:].reshape(-1)
+        loss = fused_head_loss(hidden.reshape(-1, hidden.shape[-1]), self.model.lm_head.weight,
+                               shift, None, n_labelled=n_labelled)[0]
+        loss.backward()
+        self.optimizer.step()
+        self.optimizer.zero_grad(set_to_none=True)
+        return loss.detach()
+
+
+def labelled_count(labels):
+    """Host count of the shifted targets >= 0 of a [B, S] label batch (the head's n_labelled)."""
+    return int((labels[:, 1:] >= 0).sum())

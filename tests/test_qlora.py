@@ -131,6 +131,24 @@ def test_step_equals_plain_linear_twin_on_cpu(monkeypatch):
             assert torch.equal(a, b), na
 
 
+def test_prepared_mask_gives_the_decoder_the_same_output(monkeypatch):
+    """The 4-D mask the graphed step passes equals what transformers builds from the [B, S] mask:
+    the same hidden states, bit for bit (pad rows included)."""
+    monkeypatch.setattr(qgroup, "launch", _oracle_launch)
+    model = qlora.build_model(qlora.qwen25_15b_config(**TINY), "cpu", seed=3, lora_dropout=0.0,
+                              lora_b_std=0.02)
+    qlora.patch()
+    batch = qlora.make_batch(3, 40, TINY["vocab_size"], "cpu", seed=2)
+    with torch.no_grad():
+        two = model.model(input_ids=batch["input_ids"], attention_mask=batch["attention_mask"],
+                          use_cache=False).last_hidden_state
+        four = qlora._Decoder(model)(batch["input_ids"],
+                                     qlora.causal_padding_mask(batch["attention_mask"]))
+    assert torch.equal(two, four)
+    assert qlora.labelled_count(batch["labels"]) == int(
+        (torch.nn.functional.pad(batch["labels"], (0, 1), value=-100)[:, 1:] >= 0).sum())
+
+
 def test_train_step_reduces_the_loss_with_dropout(monkeypatch):
     monkeypatch.setattr(qgroup, "launch", _oracle_launch)
     model = qlora.build_model(qlora.qwen25_15b_config(**TINY), "cpu", seed=2, lora_dropout=0.1)
@@ -178,3 +196,26 @@ def test_step_on_the_gpu_matches_the_dense_twin():
                     p.add_(p.grad, alpha=-1e-2)
                     p.grad = None
     assert RAN["head"] >= 2 and RAN["group"] + RAN["split"] > 0
+
+
+@pytest.mark.gpu
+def test_graphed_step_matches_the_eager_step():
+    """The step with the decoder replayed as CUDA graphs gives the eager step's losses and
+    adapters over three steps (the same kernels in the same order; dropout off)."""
+    config = qlora.qwen25_15b_config(**TINY)
+    kw = dict(seed=11, lora_dropout=0.0, lora_b_std=0.02)
+    eager, graphed = qlora.build_model(config, "cuda", **kw), qlora.build_model(config, "cuda", **kw)
+    qlora.patch()
+    eager.train()
+    graphed.train()
+    batch = qlora.make_batch(4, 128, TINY["vocab_size"], "cuda", seed=5)
+    n_lab = qlora.labelled_count(batch["labels"])
+    opts = [torch.optim.AdamW(qlora.adapters(m), lr=1e-3) for m in (eager, graphed)]
+    step = qlora.GraphedStep(graphed, opts[1], batch)
+    for _ in range(3):
+        a = qlora.train_step(eager, opts[0], batch)
+        b = step(batch, n_lab)
+        torch.testing.assert_close(b, a, rtol=1e-5, atol=0)
+    for (na, pa), (_, pb) in zip(eager.named_parameters(), graphed.named_parameters()):
+        if pa.requires_grad:
+            torch.testing.assert_close(pb, pa, rtol=1e-3, atol=1e-5, msg=na)
