@@ -21,8 +21,9 @@ Same line, secondary objects:
   roofline     the dominant kernel (head_slice_kernel) against the measured bf16/fp16 peak
   cpu_baseline the CPU oracle (a restatement of the reference's torch formula,
                solution/test_kernels.py:70-83) on a bounded sample, rank 0, N=1
-  c5   (--qlora, N=1) config 5: the full QLoRA step of the Qwen2.5-1.5B architecture with both
-       paths plugged in (talm_b200/qlora.py); `--only-qlora` prints it alone
+  c5   config 5 (N=1): the full QLoRA step of the Qwen2.5-1.5B architecture with both paths
+       plugged in (talm_b200/qlora.py), eager and with the decoder as CUDA graphs;
+       `--only-qlora` prints it alone, `--no-qlora` skips it
 
 `--impl reference` times the reference's CPU formula (the oracle port) on the box's host cores
 on a bounded sample per step and prints the same metric with "impl": "reference"; under
@@ -70,8 +71,8 @@ def parse_args():
                    help="the NF4 part alone (profiling runs); prints its JSON object")
     p.add_argument("--nf4-layers", type=int, default=N_LAYERS,
                    help="layers in the config-3 sweep (fewer: a small case for ncu captures)")
-    p.add_argument("--qlora", action="store_true",
-                   help="add config 5 (the full QLoRA step, N=1) as the `c5` object")
+    p.add_argument("--no-qlora", action="store_true",
+                   help="skip config 5 (the full QLoRA step, N=1, the `c5` object)")
     p.add_argument("--only-qlora", action="store_true",
                    help="config 5 alone; prints its JSON object")
     return p.parse_args()
@@ -619,10 +620,13 @@ def ours(args, world, rank, local):
         if world == 1 and rank == 0:
             line["cpu_baseline"] = cpu_head_baseline(weight, c4_inputs("cuda")[0],
                                                      c4_inputs("cuda")[1])
-    if args.qlora and world == 1:
+    if world == 1 and not (args.no_qlora or args.no_secondary):
         weight = weight_full = None
         torch.cuda.empty_cache()
-        line["c5"] = run_qlora(args.steps, args.warmup)
+        try:
+            line["c5"] = run_qlora(args.steps, args.warmup)
+        except Exception as exc:  # noqa: BLE001 - a secondary object; the headline stands
+            line["c5"] = {"error": f"{type(exc).__name__}: {exc}"[:400]}
     return line
 
 
