@@ -75,6 +75,9 @@ def parse_args():
                    help="skip config 5 (the full QLoRA step, N=1, the `c5` object)")
     p.add_argument("--only-qlora", action="store_true",
                    help="config 5 alone; prints its JSON object")
+    p.add_argument("--qlora-breakdown", action="store_true",
+                   help="add a per-kernel device-time breakdown of the config-5 step "
+                        "(torch.profiler, CUDA activity; not a timing)")
     return p.parse_args()
 
 
@@ -264,7 +267,44 @@ def nf4_layer(seed, device, double_quant):
             "offset2": torch.cat(offsets), "out": out, "n": n}
 
 
-def run_qlora(steps, warmup, batch=4, seq=512):
+_KERNEL_KINDS = (("talm head", ("talm::head",)), ("talm nf4", ("nf4_",)),
+                 ("attention", ("sdpa", "fmha", "flash", "attention")),
+                 ("gemm", ("nvjet", "gemm", "cutlass", "xmma", "cublas")),
+                 ("optimizer", ("multi_tensor", "adam")),
+                 ("copy / cat", ("catarray", "copy")),
+                 ("reduce", ("reduce",)),
+                 ("elementwise", ("elementwise", "dropout", "silu")))
+
+
+def kernel_breakdown(fn, reps=3):
+    """Device time per step by kernel kind and the 15 largest kernels, from torch.profiler's
+    CUDA activity over `reps` calls of fn (a breakdown, not a timing: the profiler adds its own
+    overhead)."""
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize()
+    kinds, rows, total, count = {}, [], 0.0, 0.0
+    for e in prof.key_averages():
+        ms = e.device_time_total / reps / 1000.0
+        if ms <= 0:
+            continue
+        name = e.key.lower()
+        kind = next((k for k, words in _KERNEL_KINDS if any(w in name for w in words)), "other")
+        kinds[kind] = kinds.get(kind, 0.0) + ms
+        total += ms
+        count += e.count / reps
+        rows.append((ms, e.count / reps, e.key[:80]))
+    rows.sort(reverse=True)
+    return {"kernel_ms_per_step": total, "kernels_per_step": count,
+            "ms_by_kind": {k: round(v, 3) for k, v in sorted(kinds.items(), key=lambda x: -x[1])},
+            "top": [[round(ms, 3), round(n, 1), k] for ms, n, k in rows[:15]]}
+
+
+def run_qlora(steps, warmup, batch=4, seq=512, breakdown=False):
     """Config 5: one QLoRA training step of the Qwen2.5-1.5B architecture (random init, NF4 base
     weights, LoRA r=16 alpha=32 on q_proj / v_proj) on a 4 x 512 batch with ~45% trailing pad,
     both hot paths plugged in (talm_b200.qlora). Step = forward with labels + backward + AdamW
@@ -291,6 +331,7 @@ def run_qlora(steps, warmup, batch=4, seq=512):
     prof = profile_kernels(step, steps)
     n_tok = batch * seq
     n_lab = qlora.labelled_count(data["labels"])
+    kinds = {"eager": kernel_breakdown(step)} if breakdown else {}
 
     # the same step with the decoder's forward and backward replayed as CUDA graphs
     try:
@@ -307,6 +348,8 @@ def run_qlora(steps, warmup, batch=4, seq=512):
                    "host_ms_per_step": HOST_MS.get("qlora_graphed"),
                    "eager_kernels_ms_per_step": {k: v[0] / steps for k, v in gprof.items()
                                                  if v[1]}}
+        if breakdown:
+            kinds["graphed"] = kernel_breakdown(graphed_step)
         del gstep
     except Exception as exc:  # noqa: BLE001 - reported in the line, the eager number stands
         graphed = {"error": f"{type(exc).__name__}: {exc}"[:400]}
@@ -323,7 +366,7 @@ def run_qlora(steps, warmup, batch=4, seq=512):
             "loss_first_last": [loss[0], loss[-1]],
             "kernels_ms_per_step": {k: v[0] / steps for k, v in prof.items() if v[1]},
             "launches_per_step": {k: v[1] / steps for k, v in prof.items() if v[1]},
-            "graphed": graphed}
+            "graphed": graphed, **({"breakdown": kinds} if breakdown else {})}
 
 
 # ------------------------------------------------------------------------------------------
@@ -624,7 +667,7 @@ def ours(args, world, rank, local):
         weight = weight_full = None
         torch.cuda.empty_cache()
         try:
-            line["c5"] = run_qlora(args.steps, args.warmup)
+            line["c5"] = run_qlora(args.steps, args.warmup, breakdown=args.qlora_breakdown)
         except Exception as exc:  # noqa: BLE001 - a secondary object; the headline stands
             line["c5"] = {"error": f"{type(exc).__name__}: {exc}"[:400]}
     return line
@@ -679,7 +722,7 @@ def main():
         elif args.only_qlora:
             if world != 1:
                 raise SystemExit("--only-qlora runs on one GPU")
-            line = {"c5": run_qlora(args.steps, args.warmup)}
+            line = {"c5": run_qlora(args.steps, args.warmup, breakdown=args.qlora_breakdown)}
         else:
             line = ours(args, world, rank, local)
         if rank == 0:
