@@ -350,23 +350,63 @@ def run_qlora(steps, warmup, batch=4, seq=512, breakdown=False):
                                                  if v[1]}}
         if breakdown:
             kinds["graphed"] = kernel_breakdown(graphed_step)
-        del gstep
     except Exception as exc:  # noqa: BLE001 - reported in the line, the eager number stands
+        gstep = None
         graphed = {"error": f"{type(exc).__name__}: {exc}"[:400]}
+
+    # the real tokens only (padding removed on the host, block-causal mask), eager and graphed
+    try:
+        host = qlora.make_batch(batch, seq, VOCAB, "cpu", seed=0)
+        t0 = time.perf_counter()
+        packed = qlora.pack_batch(host, "cuda")
+        pack_ms = (time.perf_counter() - t0) * 1000
+
+        def packed_step():
+            losses.append(qlora.packed_train_step(model, opt, packed))
+
+        for _ in range(warmup):
+            packed_step()
+        pms = timed(packed_step, steps, 1, "qlora_packed")
+        if gstep is None:
+            gstep = qlora.GraphedStep(model, opt)
+
+        def packed_graphed_step():
+            losses.append(gstep.packed(packed))
+
+        for _ in range(warmup):
+            packed_graphed_step()
+        pgms = timed(packed_graphed_step, steps, 1, "qlora_packed_graphed")
+        if breakdown:
+            kinds["packed_graphed"] = kernel_breakdown(packed_graphed_step)
+        packed_line = {"tokens_real": packed["n_real"],
+                       "tokens_packed": int(packed["input_ids"].shape[1]),
+                       "pack_batch_host_ms": pack_ms,
+                       "eager_ms_per_step": pms / steps,
+                       "eager_host_ms_per_step": HOST_MS.get("qlora_packed"),
+                       "graphed_ms_per_step": pgms / steps,
+                       "graphed_host_ms_per_step": HOST_MS.get("qlora_packed_graphed"),
+                       "graphed_tokens_per_s": n_tok / (pgms / steps / 1000)}
+    except Exception as exc:  # noqa: BLE001 - reported in the line
+        packed_line = {"error": f"{type(exc).__name__}: {exc}"[:400]}
+    del gstep
     loss = [float(x) for x in losses]
     mem = torch.cuda.max_memory_allocated() / 2**30
     del model, opt
     torch.cuda.empty_cache()
     return {"workload": "config 5: QLoRA step of Qwen2.5-1.5B (random init, NF4 double-quant "
-                        "base, LoRA r=16 alpha=32 on q/v), batch 4 x 512, ~45% trailing pad "
-                        "(padded batch with attention mask, not varlen-packed), fp16, 1 GPU",
+                        "base, LoRA r=16 alpha=32 on q/v), batch 4 x 512, ~45% trailing pad, "
+                        "fp16, 1 GPU; the padded batch (attention mask) eager and graphed, and "
+                        "`packed`: the real tokens only (padding removed on the host, "
+                        "block-causal mask), eager and graphed; tokens/s counts the 2048 batch "
+                        "positions",
             "ms_per_step": ms / steps, "tokens_per_s": n_tok / (ms / steps / 1000),
             "labelled_tokens": n_lab, "host_ms_per_step": HOST_MS.get("qlora"),
             "build_s": build_s, "max_allocated_GiB": mem,
             "loss_first_last": [loss[0], loss[-1]],
             "kernels_ms_per_step": {k: v[0] / steps for k, v in prof.items() if v[1]},
             "launches_per_step": {k: v[1] / steps for k, v in prof.items() if v[1]},
-            "graphed": graphed, **({"breakdown": kinds} if breakdown else {})}
+            "graphed": graphed, "packed": packed_line,
+            **({"breakdown": kinds} if breakdown else {})}
 
 
 # ------------------------------------------------------------------------------------------

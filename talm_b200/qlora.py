@@ -237,36 +237,116 @@ def causal_padding_mask(attention_mask):
 
 
 class _Decoder(torch.nn.Module):
-    """input ids + prepared 4-D mask -> last hidden state of the model's decoder."""
+    """input ids + prepared 4-D mask (+ position ids) -> last hidden state of the decoder."""
 
     def __init__(self, model):
         super().__init__()
         self.decoder = model.model
 
-    def forward(self, input_ids, mask4d):
-        return self.decoder(input_ids=input_ids, attention_mask=mask4d,
+    def forward(self, input_ids, mask4d, position_ids=None):
+        return self.decoder(input_ids=input_ids, attention_mask=mask4d, position_ids=position_ids,
                             use_cache=False).last_hidden_state
+
+
+def pack_batch(batch, device, bucket=256):
+    """The real tokens of a right-padded HOST batch packed into one sequence, built on the host
+    (where the collator has the batch) so that the device sees no data-dependent shape and no
+    host sync: the reference's padding removal (solution/unpad.py:66-95) does the same gather on
+    the device after one host read of the row lengths.
+
+    Row b's first len_b tokens follow one another in row order; each keeps its position in its
+    row (the rotary positions of the padded batch) and its next-token target within the row
+    (the padded batch's shifted label: the last real token's target is the pad's -100). The
+    packed length is rounded up to a multiple of `bucket` with filler tokens (id 0, target
+    -100, a segment of their own), so that a few captured graphs serve every batch. Returns
+    device tensors input_ids [1, T], position_ids [1, T], segments [T] and targets [T], and the
+    host counts n_real and n_labelled."""
+    ids, mask, labels = batch["input_ids"], batch["attention_mask"], batch["labels"]
+    if ids.is_cuda or mask.is_cuda or labels.is_cuda:
+        raise ValueError("pack_batch packs the host batch (before it is copied to the GPU)")
+    rows, seq = ids.shape
+    keep = mask.bool()
+    shift = F.pad(labels, (0, 1), value=-100)[:, 1:]
+    pos = torch.arange(seq).expand(rows, seq)
+    seg = torch.arange(rows)[:, None].expand(rows, seq)
+    real_ids, real_pos, real_seg, real_tgt = ids[keep], pos[keep], seg[keep], shift[keep]
+    n_real = int(real_ids.numel())
+    total = -(-n_real // bucket) * bucket if bucket else n_real
+    fill = total - n_real
+    packed = {
+        "input_ids": torch.cat([real_ids, torch.zeros(fill, dtype=ids.dtype)])[None],
+        "position_ids": torch.cat([real_pos, torch.arange(fill)])[None],
+        "segments": torch.cat([real_seg, torch.full((fill,), rows)]),
+        "targets": torch.cat([real_tgt, torch.full((fill,), -100, dtype=labels.dtype)]),
+    }
+    n_labelled = int((packed["targets"] >= 0).sum())
+    out = {k: v.to(device, non_blocking=True) for k, v in packed.items()}
+    out.update(n_real=n_real, n_labelled=n_labelled)
+    return out
+
+
+def block_causal_mask(segments):
+    """[1, 1, T, T] bool: token i sees token j when j <= i and both are in the same segment (a
+    row of the packed batch)."""
+    same = segments[:, None] == segments[None, :]
+    return (same & torch.ones_like(same).tril())[None, None]
+
+
+def _packed_loss(model, hidden, packed):
+    from .fused_head import fused_head_loss
+
+    return fused_head_loss(hidden.reshape(-1, hidden.shape[-1]), model.lm_head.weight,
+                           packed["targets"], None, n_labelled=packed["n_labelled"])[0]
+
+
+def packed_train_step(model, optimizer, packed):
+    """The training step on a packed batch (`pack_batch`): the decoder over the real tokens only,
+    the fused head over their targets, backward, one optimizer step."""
+    hidden = _Decoder(model)(packed["input_ids"], block_causal_mask(packed["segments"]),
+                             packed["position_ids"])
+    loss = _packed_loss(model, hidden, packed)
+    loss.backward()
+    optimizer.step()
+    optimizer.zero_grad(set_to_none=True)
+    return loss.detach()
 
 
 class GraphedStep:
     """The training step with the decoder's forward and backward replayed as CUDA graphs.
 
     The decoder (embedding, 28 layers, final norm) issues thousands of small launches per step
-    from Python; captured once for the batch shape (`torch.cuda.make_graphed_callables`), each
+    from Python; captured once per input shape (`torch.cuda.make_graphed_callables`), each
     direction is one graph launch. Inside the graphs every layer still dequantises its seven
     weights with one grouped launch per pass. The head stays eager: its row compaction depends
     on the batch's labelled count (`n_labelled`, taken from the host batch, so no host sync),
     and it is a handful of launches. The optimizer step runs eagerly after the backward.
-    Batches must keep the captured shape; the LayerGroups' pass bookkeeping runs during the
+    Padded batches (`__call__`) must keep the shape of `batch`, captured at construction;
+    packed batches (`packed`) capture one graph pair per packed length (a multiple of
+    pack_batch's bucket) on first use. The LayerGroups' pass bookkeeping runs during each
     capture and the graphs replay its launches."""
 
-    def __init__(self, model, optimizer, batch, warmup=3):
-        self.model, self.optimizer = model, optimizer
-        ids, mask = batch["input_ids"], batch["attention_mask"]
-        self.shape = tuple(ids.shape)
-        self.decoder = torch.cuda.make_graphed_callables(
-            _Decoder(model), (ids.clone(), causal_padding_mask(mask)),
-            num_warmup_iters=warmup)
+    def __init__(self, model, optimizer, batch=None, warmup=3):
+        self.model, self.optimizer, self.warmup = model, optimizer, warmup
+        self.graphs = {}
+        self.shape = None
+        if batch is not None:
+            ids, mask = batch["input_ids"], batch["attention_mask"]
+            self.shape = tuple(ids.shape)
+            self._graph(("padded", self.shape), (ids, causal_padding_mask(mask)))
+
+    def _graph(self, key, args):
+        if key not in self.graphs:
+            # the sample arguments become the graphs' static inputs: copies, not the caller's
+            self.graphs[key] = torch.cuda.make_graphed_callables(
+                _Decoder(self.model), tuple(a.clone() for a in args),
+                num_warmup_iters=self.warmup)
+        return self.graphs[key]
+
+    def _finish(self, loss):
+        loss.backward()
+        self.optimizer.step()
+        self.optimizer.zero_grad(set_to_none=True)
+        return loss.detach()
 
     def __call__(self, batch, n_labelled):
         ids, mask, labels = batch["input_ids"], batch["attention_mask"], batch["labels"]
@@ -274,14 +354,18 @@ class GraphedStep:
             raise ValueError(f"batch shape {tuple(ids.shape)} is not the captured {self.shape}")
         from .fused_head import fused_head_loss
 
-        hidden = self.decoder(ids, causal_padding_mask(mask))
+        hidden = self.graphs[("padded", self.shape)](ids, causal_padding_mask(mask))
         shift = F.pad(labels, (0, 1), value=-100)[:, 1:].reshape(-1)
         loss = fused_head_loss(hidden.reshape(-1, hidden.shape[-1]), self.model.lm_head.weight,
                                shift, None, n_labelled=n_labelled)[0]
-        loss.backward()
-        self.optimizer.step()
-        self.optimizer.zero_grad(set_to_none=True)
-        return loss.detach()
+        return self._finish(loss)
+
+    def packed(self, packed):
+        """One step on a packed batch (`pack_batch`)."""
+        args = (packed["input_ids"], block_causal_mask(packed["segments"]),
+                packed["position_ids"])
+        graph = self._graph(("packed", tuple(packed["input_ids"].shape)), args)
+        return self._finish(_packed_loss(self.model, graph(*args), packed))
 
 
 def labelled_count(labels):

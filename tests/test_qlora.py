@@ -149,6 +149,55 @@ def test_prepared_mask_gives_the_decoder_the_same_output(monkeypatch):
         (torch.nn.functional.pad(batch["labels"], (0, 1), value=-100)[:, 1:] >= 0).sum())
 
 
+def test_pack_batch_keeps_each_rows_tokens_positions_and_targets():
+    batch = qlora.make_batch(4, 64, TINY["vocab_size"], "cpu", seed=6)
+    packed = qlora.pack_batch(batch, "cpu", bucket=32)
+    mask, ids = batch["attention_mask"].bool(), batch["input_ids"]
+    shift = torch.nn.functional.pad(batch["labels"], (0, 1), value=-100)[:, 1:]
+    n_real = int(mask.sum())
+    total = packed["input_ids"].shape[1]
+    assert packed["n_real"] == n_real and total % 32 == 0 and total - n_real < 32
+    at = 0
+    for row in range(4):
+        n = int(mask[row].sum())
+        assert torch.equal(packed["input_ids"][0, at:at + n], ids[row, :n])
+        assert torch.equal(packed["position_ids"][0, at:at + n], torch.arange(n))
+        assert torch.equal(packed["targets"][at:at + n], shift[row, :n])
+        assert int(packed["targets"][at + n - 1]) == -100
+        assert (packed["segments"][at:at + n] == row).all()
+        at += n
+    assert (packed["targets"][at:] == -100).all() and (packed["segments"][at:] == 4).all()
+    assert packed["n_labelled"] == int((shift >= 0).sum())
+
+
+def test_packed_decoder_matches_the_padded_rows(monkeypatch):
+    """The decoder over the packed real tokens (block-causal mask, per-row positions) gives the
+    padded batch's hidden states at the real positions, and the same next-token loss (fp16 on
+    the CPU: within fp16 rounding of differently blocked GEMMs)."""
+    monkeypatch.setattr(qgroup, "launch", _oracle_launch)
+    model = qlora.build_model(qlora.qwen25_15b_config(**TINY), "cpu", seed=8, lora_dropout=0.0,
+                              lora_b_std=0.02)
+    qlora.patch()
+    batch = qlora.make_batch(3, 48, TINY["vocab_size"], "cpu", seed=9)
+    packed = qlora.pack_batch(batch, "cpu", bucket=16)
+    with torch.no_grad():
+        padded = qlora._Decoder(model)(batch["input_ids"],
+                                       qlora.causal_padding_mask(batch["attention_mask"]))
+        flat = qlora._Decoder(model)(packed["input_ids"],
+                                     qlora.block_causal_mask(packed["segments"]),
+                                     packed["position_ids"])
+    real = flat[0, :packed["n_real"]].float()
+    ref = padded[batch["attention_mask"].bool()].float()
+    torch.testing.assert_close(real, ref, rtol=2e-2, atol=2e-2)
+    w = model.lm_head.weight.float()
+    shift = torch.nn.functional.pad(batch["labels"], (0, 1), value=-100)[:, 1:].reshape(-1)
+    loss_padded = torch.nn.functional.cross_entropy(padded.reshape(-1, padded.shape[-1]).float()
+                                                    @ w.t(), shift, ignore_index=-100)
+    loss_packed = torch.nn.functional.cross_entropy(flat[0].float() @ w.t(), packed["targets"],
+                                                    ignore_index=-100)
+    torch.testing.assert_close(loss_packed, loss_padded, rtol=1e-3, atol=0)
+
+
 def test_train_step_reduces_the_loss_with_dropout(monkeypatch):
     monkeypatch.setattr(qgroup, "launch", _oracle_launch)
     model = qlora.build_model(qlora.qwen25_15b_config(**TINY), "cpu", seed=2, lora_dropout=0.1)
@@ -219,3 +268,34 @@ def test_graphed_step_matches_the_eager_step():
     for (na, pa), (_, pb) in zip(eager.named_parameters(), graphed.named_parameters()):
         if pa.requires_grad:
             torch.testing.assert_close(pb, pa, rtol=1e-3, atol=1e-5, msg=na)
+
+
+@pytest.mark.gpu
+def test_packed_steps_match_the_padded_step():
+    """The packed step (real tokens only), eager and with the decoder as CUDA graphs, against the
+    padded eager step on the same batch: the same loss within 2e-3, adapter gradients within
+    3e-2 in relative norm; packed graphed equals packed eager."""
+    config = qlora.qwen25_15b_config(**TINY)
+    kw = dict(seed=13, lora_dropout=0.0, lora_b_std=0.02)
+    models = [qlora.build_model(config, "cuda", **kw) for _ in range(3)]
+    qlora.patch()
+    for m in models:
+        m.train()
+    host = qlora.make_batch(4, 128, TINY["vocab_size"], "cpu", seed=3)
+    batch = {k: v.cuda() for k, v in host.items()}
+    packed = qlora.pack_batch(host, "cuda", bucket=128)
+    assert packed["n_labelled"] == qlora.labelled_count(host["labels"])
+    step = qlora.GraphedStep(models[2], torch.optim.SGD(qlora.adapters(models[2]), lr=0.0))
+    out = models[0](**batch)
+    out.loss.backward()
+    eager = qlora._packed_loss(models[1], qlora._Decoder(models[1])(
+        packed["input_ids"], qlora.block_causal_mask(packed["segments"]),
+        packed["position_ids"]), packed)
+    eager.backward()
+    graphed = step.packed(packed)
+    torch.testing.assert_close(eager.detach(), out.loss.detach(), rtol=2e-3, atol=0)
+    torch.testing.assert_close(graphed, eager.detach(), rtol=1e-5, atol=0)
+    ga, gb = _grads(models[0]), _grads(models[1])
+    for name in ga:
+        err = float((gb[name] - ga[name]).norm() / ga[name].norm().clamp(min=1e-30))
+        assert err < 3e-2, (name, err)
