@@ -65,7 +65,8 @@ int talm_device_status(int* status_out);
 #define TALM_KERNEL_PEER_PUBLISH 8  /* publish_stats_kernel (peer exchange, phase 0)      */
 #define TALM_KERNEL_PEER_REDUCE 9   /* reduce_gather_kernel (peer exchange, phase 2)      */
 #define TALM_KERNEL_PEER_FINISH 10  /* gather_finish_kernel (wait + copy out)             */
-#define TALM_KERNEL_KINDS 11
+#define TALM_KERNEL_NF4_GEMM 11     /* nf4_gemm_kernel (fused NF4 dequant + tcgen05 GEMM)  */
+#define TALM_KERNEL_KINDS 12
 int talm_profile_begin(void);
 int talm_profile_end(double* ms_out, int64_t* launches_out, int n_kinds);
 
@@ -101,6 +102,27 @@ int talm_nf4_group_dequant(const uint8_t* packed, const uint8_t* absmax8, const 
                            const float* absmax2, const float* offset2, const float* levels,
                            uint16_t* out, int64_t n_rows, int64_t qblock, int64_t qblock2,
                            void* stream);
+
+/* Fused NF4 dequantisation + GEMM (tcgen05): the product of an fp16 activation with R
+ * consecutive 4-bit weight rows of a layer group, the weights rebuilt in shared memory exactly
+ * as talm_nf4_group_dequant rebuilds them, never written to HBM. Replaces the grouped path's
+ * dequant launch + cuBLAS product (solution/qgroup.py:346-355, GroupLinear):
+ *   transpose = 0: y[n_rows, w_rows] = a[n_rows, w_cols] . W^T (+ bias[w_rows])   (forward)
+ *   transpose = 1: y[n_rows, w_cols] = a[n_rows, w_rows] . W  (input gradient; bias NULL)
+ *   a, y    : fp16 rows, strides ld_a, ld_y elements (multiples of 8, 16-byte aligned bases)
+ *   packed  : w_rows * w_cols / 2 bytes, row-major (16-byte aligned)
+ *   absmax8 : w_rows * w_cols / 64 coded scales of this weight (qblock 64)
+ *   absmax2, offset2 : the group's second-level arrays, indexed by
+ *             (absmax_row0 + absmax index within this weight) / qblock2
+ *   code    : 256 fp32         levels : 16 fp32
+ * Preconditions: qblock == 64, w_rows % 64 == 0, w_cols % 128 == 0, fp32 accumulation; the
+ * output is rounded to fp16 once (after the bias). */
+int talm_nf4_linear(const uint16_t* a, int64_t ld_a, int64_t n_rows, const uint8_t* packed,
+                    const uint8_t* absmax8, const float* code, const float* absmax2,
+                    const float* offset2, const float* levels, int64_t absmax_row0,
+                    int64_t w_rows, int64_t w_cols, int64_t qblock, int64_t qblock2,
+                    int transpose, const uint16_t* bias, uint16_t* y, int64_t ld_y,
+                    void* stream);
 
 /* ------------------------------------------------------------------------------------------
  * Fused LM head + cross-entropy (vocabulary-sliced, no materialised logits)

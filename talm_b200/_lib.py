@@ -29,6 +29,8 @@ SIGNATURES = {
     "talm_profile_end": (_INT, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_I64), _INT]),
     "talm_nf4_dequantize": (_INT, [_P, _P, _I64, _I64, _P, _P]),
     "talm_nf4_group_dequant": (_INT, [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
+    "talm_nf4_linear": (_INT, [_P, _I64, _I64, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64,
+                               _I64, _INT, _P, _P, _I64, _P]),
     "talm_head_workspace_size": (_INT, [_I64, _I64, _I64, _I64, _I64, ctypes.POINTER(_SZ)]),
     "talm_head_shard": (_INT, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P,
                                _P, _P, _SZ, _P]),
@@ -100,7 +102,8 @@ def stream_of(device):
 
 
 KERNEL_KINDS = ("head_slice", "head_combine", "head_reserved", "head_finalize", "head_merge",
-                "nf4", "nf4_tail", "head_scale", "peer_publish", "peer_reduce", "peer_finish")
+                "nf4", "nf4_tail", "head_scale", "peer_publish", "peer_reduce", "peer_finish",
+                "nf4_gemm")
 
 
 def profile_begin():

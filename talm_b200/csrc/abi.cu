@@ -97,7 +97,8 @@ static EncodeTiledFn encode_fn() {
 
 static int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, uint64_t elem_bytes,
                         const void* base, uint64_t inner, uint64_t outer,
-                        uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer);
+                        uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
+                        CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 int talm_make_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                           uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer) {
@@ -113,7 +114,8 @@ int talm_make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t inner, ui
 
 static int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, uint64_t elem_bytes,
                         const void* base, uint64_t inner, uint64_t outer,
-                        uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer) {
+                        uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
+                        CUtensorMapSwizzle swizzle) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return talm::set_error(TALM_ENODEV, "cuTensorMapEncodeTiled unavailable");
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
@@ -126,7 +128,7 @@ static int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, uint64_t el
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return talm::set_error(TALM_EINVAL, "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu",

@@ -278,6 +278,45 @@ class LayerGroup:
         return self._span_biases[key]
 
 
+def _span(group, first, last):
+    """The packed bytes, coded scales, group-wide first absmax row and [rows, cols] of the
+    adjacent projections first .. last - 1 (one weight of sum-of-rows x shared columns)."""
+    cols = group.shapes[first][1]
+    if any(group.shapes[i][1] != cols for i in range(first, last)):
+        raise ValueError("projections of a span share their input size")
+    rows = sum(group.shapes[i][0] for i in range(first, last))
+    b0, b1 = group.pair_bounds[first], group.pair_bounds[last]
+    r0, r1 = group.row_bounds[first], group.row_bounds[last]
+    return group.packed[b0:b1], group.absmax8[r0:r1], r0, rows, cols
+
+
+def fused_linear(x, group, first, last=None, bias=None, transpose=False):
+    """The fused NF4 dequant + tcgen05 GEMM (talm_nf4_linear) on projections first .. last - 1
+    of `group` (default: `first` alone): x [..., in] -> x W^T (+ bias) [..., sum of out], or with
+    transpose=True the input gradient g [..., sum of out] -> g W [..., in]. The weights are
+    rebuilt in shared memory bit for bit as the grouped kernel writes them (the same fp16
+    values F.linear would read from the dequantised buffer); the products accumulate in fp32.
+    Needs qblock 64, spans of 64-row multiples and input sizes of 128-column multiples."""
+    last = first + 1 if last is None else last
+    packed, absmax8, row0, rows, cols = _span(group, first, last)
+    red, n_out = (rows, cols) if transpose else (cols, rows)
+    if x.shape[-1] != red:
+        raise ValueError(f"last dimension {x.shape[-1]}, expected {red}")
+    a = x.reshape(-1, red)
+    if a.dtype != torch.float16 or a.stride(1) != 1 or a.stride(0) % 8 or a.data_ptr() % 16:
+        a = a.to(torch.float16).contiguous()
+    y = torch.empty(a.shape[0], n_out, dtype=torch.float16, device=a.device)
+    if bias is not None:
+        bias = bias.to(torch.float16).contiguous()
+    lib = _lib.load()
+    _lib.check(lib.talm_nf4_linear(
+        _lib.ptr(a), a.stride(0), a.shape[0], _lib.ptr(packed), _lib.ptr(absmax8),
+        _lib.ptr(group.code), _lib.ptr(group.absmax2), _lib.ptr(group.offset2),
+        _lib.ptr(group.levels), row0, rows, cols, group.qblock, group.qblock2, int(transpose),
+        _lib.ptr(bias), _lib.ptr(y), y.stride(0), _lib.stream_of(a.device)), "talm_nf4_linear")
+    return y.view(*x.shape[:-1], n_out)
+
+
 class GroupLinear(torch.autograd.Function):
     """x @ W^T (+ b) with W from the layer's dequantised buffer; the frozen weight gets no
     gradient (solution/qgroup.py:346-355)."""

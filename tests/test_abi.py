@@ -117,3 +117,21 @@ def test_peer_exchange_and_backward_reject_bad_arguments(lib):
 def test_labelled_first_rejects_bad_arguments(lib):
     assert lib.talm_head_labelled_first(None, 4, 5, None, 8, 8, None, None, None, None, None) == 1
     assert lib.talm_head_labelled_first(None, 0, 0, None, 8, 8, None, None, None, None, None) == 0
+
+
+def test_fused_nf4_gemm_rejects_bad_arguments(lib):
+    """talm_nf4_linear validates its shapes before it touches a pointer or the device."""
+    def call(n_rows=8, qblock=64, rows=128, cols=256, transpose=0, bias=None, ld_a=256,
+             ld_y=128, qblock2=256):
+        return lib.talm_nf4_linear(None, ld_a, n_rows, None, None, None, None, None, None, 0,
+                                   rows, cols, qblock, qblock2, transpose, bias, None, ld_y, None)
+    assert call(qblock=128) == 1                 # qblock 64 only
+    assert call(rows=96) == 1                    # rows: multiples of 64
+    assert call(cols=192) == 1                   # columns: multiples of 128
+    assert call(transpose=1, bias=16, ld_a=128, ld_y=256) == 1   # no bias on the gradient
+    assert call(ld_a=200) == 1                   # stride below the reduction length
+    assert call(ld_y=100) == 1                   # stride not a multiple of 8
+    assert call(qblock2=0) == 1
+    assert call(n_rows=-1) == 1
+    assert call(n_rows=0) == 0                   # nothing to do: no pointer read
+    assert b"qblock" in (call(qblock=32) and lib.talm_last_error())

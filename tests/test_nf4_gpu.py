@@ -220,3 +220,35 @@ def test_group_linear_launches_once_per_pass(monkeypatch):
     sum((F.linear(inp, w).float() ** 2).mean()
         for inp, w in zip([x2] * 6 + [h2], refs)).backward()
     assert torch.equal(x.grad, x2.grad) and torch.equal(h.grad, h2.grad)
+
+
+@pytest.mark.parametrize("n_tokens", [2048, 37])
+def test_fused_linear_matches_dequant_and_cublas(n_tokens):
+    """The fused NF4 dequant + tcgen05 GEMM (talm_nf4_linear) on the Qwen layer's spans (q|k|v
+    with bias, o, gate|up, down, k alone), forward and input gradient, against F.linear / matmul
+    on the grouped kernel's dequantised weights. Both accumulate in fp32 and round once to fp16;
+    they agree to an fp16 ulp (measured: bit-identical on almost every element)."""
+    from talm_b200 import _lib
+    from talm_b200.qgroup import LayerGroup, fused_linear
+
+    mods, _, _ = _qwen_layer(5)
+    group = LayerGroup(mods)
+    full = group.dequantize_all()
+    torch.manual_seed(1)
+    for first, last in ((0, 3), (3, 4), (4, 6), (6, 7), (1, 2)):
+        rows = sum(group.shapes[i][0] for i in range(first, last))
+        cols = group.shapes[first][1]
+        w = full[group.elem_bounds[first]:group.elem_bounds[last]].view(rows, cols)
+        x = torch.randn(n_tokens, cols, device=DEV, dtype=torch.float16)
+        bias = (torch.randn(rows, device=DEV) * 0.1).half() if first == 0 else None
+        ref = F.linear(x, w, bias)
+        out = fused_linear(x, group, first, last, bias=bias)
+        torch.testing.assert_close(out.float(), ref.float(), rtol=2e-3,
+                                   atol=float(ref.abs().max()) * 1e-3)
+        g = torch.randn(n_tokens, rows, device=DEV, dtype=torch.float16)
+        ref = g @ w
+        out = fused_linear(g, group, first, last, transpose=True)
+        torch.testing.assert_close(out.float(), ref.float(), rtol=2e-3,
+                                   atol=float(ref.abs().max()) * 1e-3)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
