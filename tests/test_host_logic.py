@@ -178,3 +178,21 @@ def test_apply_installs_what_is_importable():
         assert modeling_qwen2.Qwen2ForCausalLM.forward is patched
     finally:
         modeling_qwen2.Qwen2ForCausalLM.forward = before
+
+
+def test_fused_linear_checks_the_span_before_any_launch(golden_dir):
+    """qgroup.fused_linear refuses spans whose projections differ in input size and inputs of
+    the wrong width on the host (CPU tensors: nothing reaches the library)."""
+    g = np.load(os.path.join(golden_dir, "nf4_group.npz"))
+    group = qgroup.LayerGroup(_modules_from_golden(g))
+    # golden shapes: six projections of 256 inputs, the last of 512
+    with pytest.raises(ValueError, match="share"):
+        qgroup.fused_linear(torch.zeros(4, 256, dtype=torch.float16), group, 5, 7)
+    with pytest.raises(ValueError, match="last dimension"):
+        qgroup.fused_linear(torch.zeros(4, 128, dtype=torch.float16), group, 0, 2)
+    with pytest.raises(ValueError, match="last dimension"):
+        qgroup.fused_linear(torch.zeros(4, 256, dtype=torch.float16), group, 0, 2,
+                            transpose=True)
+    packed, absmax8, row0, rows, cols = qgroup._span(group, 4, 6)
+    assert (rows, cols) == (256, 256) and row0 == group.row_bounds[4]
+    assert packed.numel() == rows * cols // 2 and absmax8.numel() == rows * cols // 64
