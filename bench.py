@@ -135,21 +135,34 @@ def max_over_ranks(value, world):
 HOST_MS = {}  # host time to issue the timed loop, per timed() label (diagnostic only)
 
 
-def timed(fn, steps, world, label=None):
+KERNELS = {}  # per timed() label: {kind: (device ms, launches)} of the library's own launches
+
+
+def timed(fn, steps, world, label=None, kernels=False):
     """Device time of `steps` calls of fn (CUDA events on the current stream, barrier and
     synchronize on both sides), max over ranks, in ms. With `label`, the host time spent
     issuing the loop (before the closing synchronize) is kept in HOST_MS: when it is close to
-    the device time, the step is bound by the host, not the GPU."""
+    the device time, the step is bound by the host, not the GPU. With `kernels`, every launch of
+    the library inside the timed region is bracketed by its own pair of CUDA events on its
+    stream (talm_profile_begin/_end) and KERNELS[label] gets the per-kind device times of this
+    same region: they partition (part of) the measured time, and the events' own cost is
+    inside it."""
+    from talm_b200 import _lib
+
     barrier(world)
     start = torch.cuda.Event(enable_timing=True)
     stop = torch.cuda.Event(enable_timing=True)
     start.record()
+    if kernels:
+        _lib.profile_begin()
     t0 = time.perf_counter()
     for _ in range(steps):
         fn()
     host = (time.perf_counter() - t0) * 1000
     stop.record()
     barrier(world)
+    if kernels:
+        KERNELS[label] = _lib.profile_end()
     if label is not None:
         HOST_MS[label] = max_over_ranks(host, world) / steps
     return max_over_ranks(start.elapsed_time(stop), world)
@@ -484,9 +497,9 @@ def run_head(world, rank, local, steps, warmup, hidden, weight, targets, clocks_
     for _ in range(warmup):
         step()
     sampler = ClockSampler(clocks_on and rank == 0)
-    ms = timed(step, steps, world, "head")
+    ms = timed(step, steps, world, "head", kernels=True)
     clocks = sampler.stop(set(range(world))) if rank == 0 else None
-    prof = profile_kernels(step, steps)
+    prof = KERNELS["head"]
     graph = graph_ms_per_step(step, steps, warmup) if world == 1 else None
     return {"ms_per_step": ms / steps, "n_tokens": n_tokens, "n_labelled": n_lab,
             "clocks": clocks, "kernels": prof, "host_ms_per_step": HOST_MS.get("head"),
@@ -550,7 +563,9 @@ def run_nf4(world, rank, steps, warmup, n_layers=N_LAYERS):
                              "grouped launch per layer, layers sharded contiguously over the ranks",
                  "GB_per_s": total_bytes / (ms / steps) / 1e6, "ms_per_sweep": ms / steps,
                  "bytes_per_sweep": total_bytes,
-                 "kernel_us_per_layer": 1000 * k_ms / max(k_n, 1)}
+                 "kernel_us_per_layer": 1000 * k_ms / max(k_n, 1),
+                 "kernel_us_source": "a second pass of the same sweep with one CUDA event pair "
+                                     "per launch (the timed region itself has none)"}
     del layers
     if world == 1:
         # config 1: fp32 absmax, one launch per layer over its concatenated buffers; eight
@@ -581,6 +596,63 @@ def run_nf4(world, rank, steps, warmup, n_layers=N_LAYERS):
     return res
 
 
+def parity_check(world, rank, hidden, weight_full, weight, targets, col0):
+    """Outside the timed region: the headline's head against an independent computation on the
+    same inputs. N > 1: the vocabulary-parallel head (this rank's shard) against the single-GPU
+    fused head on the full weight (every rank holds it before sharding) - loss, per-token loss
+    and entropy within 1e-5, correctness exact, dH within rtol 1e-3 + 2^-10 max|dH| (the
+    tolerances of tests/test_vocab_parallel_gpu.py). N = 1: the first 64 rows through
+    fused_head_loss against the CPU oracle (the reference's formula, oracle.head.reference_head)
+    with the reference's own tolerances (loss 1e-4, per-token 1e-4, dH rtol 1e-3). The flags and
+    worst errors are reduced over the ranks."""
+    from talm_b200.fused_head import fused_head_loss
+    from talm_b200.vocab_parallel import vocab_parallel_head_loss
+
+    def run(fn, h, *a, **k):
+        x = h.detach().clone().requires_grad_(True)
+        out = fn(x, *a, **k)
+        out[0].backward()
+        return [t.detach() for t in out], x.grad
+
+    if world > 1:
+        n_lab = int((targets >= 0).sum())
+        got, g = run(vocab_parallel_head_loss, hidden, weight, targets, VOCAB, col0, None, CHUNK,
+                     n_labelled=n_lab)
+        ref, rg = run(fused_head_loss, hidden, weight_full, targets, None, CHUNK,
+                      n_labelled=n_lab)
+        tol = (1e-5, 1e-5)
+        what = "vocab-parallel head vs the single-GPU head on the full weight, all rows"
+    else:
+        from oracle.head import reference_head
+
+        rows = 64
+        got, g = run(fused_head_loss, hidden[:rows], weight, targets[:rows], None, CHUNK)
+        r = reference_head(hidden[:rows].cpu(), weight.cpu(), targets[:rows].cpu())
+        ref = [t.to(hidden.device) for t in r[:4]]
+        rg = r[4].to(hidden.device)
+        tol = (1e-4, 1e-4)
+        what = f"fused_head_loss vs the CPU oracle (reference_head), first {rows} rows"
+    loss_rel = float(((got[0].float() - ref[0].float()).abs() / ref[0].float().abs()).item())
+    tl_excess = float(((got[1] - ref[1]).abs() - tol[1] * (1 + ref[1].abs())).max().item())
+    ent_excess = float(((got[2] - ref[2]).abs() - tol[1] * (1 + ref[2].abs())).max().item())
+    mismatches = int((got[3].bool() != ref[3].bool()).sum().item())
+    gf, rgf = g.float(), rg.float()
+    bound = 1e-3 * rgf.abs() + float(rgf.abs().max()) * 2 ** -10
+    grad_excess = float(((gf - rgf).abs() - bound).max().item())
+    ok = (loss_rel <= tol[0] and tl_excess <= 0 and ent_excess <= 0 and mismatches == 0
+          and grad_excess <= 0)
+    vals = torch.tensor([0.0 if ok else 1.0, loss_rel, tl_excess, ent_excess, float(mismatches),
+                         grad_excess], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    v = vals.tolist()
+    return {"ok": v[0] == 0.0, "what": what, "ranks": world, "loss_rel_err": v[1],
+            "token_loss_excess": v[2], "entropy_excess": v[3], "correct_mismatches": int(v[4]),
+            "grad_excess": v[5],
+            "tolerances": {"loss_rel": tol[0], "per_token": tol[1], "grad_rtol": 1e-3,
+                           "grad_atol": "2^-10 max|dH|"}}
+
+
 def cpu_head_baseline(weight, hidden, targets, budget_s=12.0):
     """The oracle (torch CPU restatement of the reference's head formula) on a bounded sample of
     the workload's rows against the full vocabulary; tokens/s."""
@@ -607,15 +679,18 @@ def ours(args, world, rank, local):
     pk = peaks()
     weight_full = head_weight("cuda")
     hidden, targets = c4_inputs("cuda")
+    col0 = 0
     if world > 1:
         from talm_b200.vocab_parallel import shard_bounds
 
         col0, cols = shard_bounds(VOCAB, world, rank)
         weight = weight_full[col0:col0 + cols].contiguous()
-        del weight_full
-        torch.cuda.empty_cache()
     else:
         weight = weight_full
+    parity = parity_check(world, rank, hidden, weight_full, weight, targets, col0)
+    if world > 1:
+        del weight_full
+        torch.cuda.empty_cache()
     head = run_head(world, rank, local, args.steps, args.warmup, hidden, weight, targets, True)
     e2e_ms, h2d, d2h = run_head_e2e(world, rank, args.steps, args.warmup, hidden, weight,
                                     targets)
@@ -623,7 +698,7 @@ def ours(args, world, rank, local):
     value = n_tok / (head["ms_per_step"] / 1000)
 
     kernels = head["kernels"]
-    total_ms = sum(v[0] for v in kernels.values()) or 1.0
+    step_ms_total = head["ms_per_step"] * args.steps
     # head_slice_kernel runs every tensor-core FLOP of the step: the logits GEMM of every row
     # and the accumulator GEMM of the labelled rows over this rank's columns; one launch per
     # slice step. achieved = algorithmic FLOPs per launch / average launch duration.
@@ -659,6 +734,9 @@ def ours(args, world, rank, local):
                      "peak_source": f"{pk['source']} bf16 sustained (kernel inside a long step)",
                      "frac_of_burst": (ach / pk["bf16_tflops"]) if ach else None,
                      "traffic": profile_traffic("head_slice_c4"),
+                     "achieved_source": "algorithmic FLOPs of the step's head_slice_kernel "
+                                        "launches / their event-timed durations in the timed "
+                                        "region",
                      "flops_per_launch": flops_per_launch,
                      "step_TFLOPs": head_flops(n_tok, n_lab) / (head["ms_per_step"] / 1000)
                      / 1e12},
@@ -668,7 +746,12 @@ def ours(args, world, rank, local):
                             * args.steps * world),
         "clocks": head["clocks"],
         "kernels": {k: {"ms_per_step": v[0] / args.steps, "launches_per_step": v[1] / args.steps,
-                        "share": v[0] / total_ms} for k, v in kernels.items() if v[1]},
+                        "share_of_step": v[0] / step_ms_total}
+                    for k, v in kernels.items() if v[1]},
+        "kernels_note": "each library launch inside the timed region bracketed by its own CUDA "
+                        "event pair on its stream (the events are inside ms_per_step); "
+                        "share_of_step = kernel time / measured step time",
+        "parity": parity,
         "host_ms_per_step": head["host_ms_per_step"],
         "graph_ms_per_step": head["graph_ms_per_step"],
     }
@@ -687,6 +770,7 @@ def ours(args, world, rank, local):
                           / (c2["ms_per_step"] / 1000) / 1e12 / pk["bf16_tflops"],
                           "kernels_ms_per_step": {k: v[0] / args.steps for k, v in k2.items()
                                                   if v[1]},
+                          "kernels_ms_sum": sum(v[0] for v in k2.values()) / args.steps,
                           "host_ms_per_step": c2["host_ms_per_step"],
                           "graph_ms_per_step": c2["graph_ms_per_step"]}
         nf4 = run_nf4(world, rank, args.steps, args.warmup, args.nf4_layers)
@@ -697,7 +781,11 @@ def ours(args, world, rank, local):
             nf4["c1"]["roofline"] = {"bound": "hbm", "achieved": nf4["c1"]["GB_per_s"],
                                      "peak": pk["hbm_gbs"], "unit": "GB/s",
                                      "frac": nf4["c1"]["GB_per_s"] / pk["hbm_gbs"],
-                                     "traffic": profile_traffic("nf4_c1_layer")}
+                                     "traffic": None,
+                                     "traffic_note": "not reported: a single-launch capture "
+                                                     "ends with most of the 93.6 MB fp16 output "
+                                                     "still in L2, so its DRAM bytes understate "
+                                                     "the launch's traffic"}
         nf4["c3"]["frac_of_hbm_per_gpu"] = nf4["c3"]["GB_per_s"] / world / pk["hbm_gbs"]
         line["nf4"] = nf4
         if world == 1 and rank == 0:
@@ -713,8 +801,12 @@ def ours(args, world, rank, local):
     return line
 
 
-def reference(args, world, rank):
-    """--impl reference: the reference's head formula on the CPU (oracle port), rank 0 only."""
+def reference(args, world, rank, step_budget_s=1.0):
+    """--impl reference: the reference's head formula on the CPU (oracle port: the torch
+    restatement of solution/test_kernels.py:70-83), all host threads, rank 0 only. Each step is
+    a bounded sample of config 4: the first n rows against the full vocabulary, n sized by a
+    probe so that one step is about `step_budget_s` of CPU work and never below 128 rows (a
+    few-row GEMM would understate what the CPU does per token)."""
     if rank != 0:
         return None
     from oracle.head import reference_head
@@ -723,7 +815,12 @@ def reference(args, world, rank):
     w = head_weight("cpu") if not torch.cuda.is_available() else head_weight("cuda").cpu()
     hidden, targets = c4_inputs("cuda") if torch.cuda.is_available() else c4_inputs("cpu")
     hidden, targets = hidden.cpu(), targets.cpu()
-    n = 8
+    probe = 32
+    reference_head(hidden[:probe], w, targets[:probe])  # first call: thread pools, page-in
+    t0 = time.perf_counter()
+    reference_head(hidden[:probe], w, targets[:probe])
+    per_row = (time.perf_counter() - t0) / probe
+    n = int(min(1024, max(128, step_budget_s / max(per_row, 1e-6)))) // 32 * 32
     times = []
     for i in range(args.warmup + args.steps):
         t0 = time.perf_counter()
@@ -736,8 +833,10 @@ def reference(args, world, rank):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": per_step * 1000, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "fp32 (fp16-rounded logits)", "data": "synthetic",
-            "config": {"workload": "config 4 rows (bounded sample) x full vocabulary on CPU",
-                       "global_batch": n, "seq_len": n, "parallelism": "cpu"},
+            "config": {"workload": f"config 4 (hidden [16384,1536], weight [151936,1536]): the "
+                                   f"first {n} rows per step x full vocabulary on the CPU",
+                       "global_batch": n, "seq_len": n, "sample_rows": n,
+                       "parallelism": "cpu"},
             "cpu_baseline": {"value": value, "unit": "tokens/s",
                              "cores": torch.get_num_threads(), "kind": "port",
                              "sample": f"{n} rows of config 4 per step x vocab {VOCAB} x "

@@ -47,6 +47,13 @@ const char* talm_status_string(int status);
  * reference counterpart: the reference's Triton kernels have no device-side waits. */
 int talm_device_status(int* status_out);
 
+/* Sets how long every bounded device-side wait of this library (pipeline barriers, the peer
+ * exchange's phase flags) spins before it gives up with TALM_ETIMEOUT, on the current device;
+ * 0 restores the default of 2 s. Synchronous (a copy to device memory): call it between
+ * launches, not while kernels of this library run. For tests that make a wait run out on
+ * purpose without a fault. No reference counterpart (the reference has no device-side waits). */
+int talm_set_wait_limit_ns(uint64_t limit_ns);
+
 /* Kernel-level timing (the counterpart of the reference's Triton launch timer,
  * harness/_train.py:44-85): between talm_profile_begin and talm_profile_end every kernel this
  * library launches is bracketed by CUDA events on its own stream. talm_profile_end synchronises

@@ -9,8 +9,8 @@ behind the reference's own Python entry points.
 
 `apply()` installs the patches of these paths the way `solution.apply()` does
 (solution/__init__.py:229-408, the steps that concern them): the grouped dequantisation of every
-decoder layer when bitsandbytes is importable (else the per-projection patch), and the fused
-head for Qwen2ForCausalLM. The kernels live in libtalm_b200.so (C ABI: include/talm.h), loaded
+decoder layer when bitsandbytes is importable (else the per-projection patch), the fused head
+for Qwen2ForCausalLM and, when trl imports, SFTTrainer.compute_loss through it. The kernels live in libtalm_b200.so (C ABI: include/talm.h), loaded
 through ctypes; there is no Triton and no CPU path.
 """
 
@@ -44,7 +44,11 @@ def apply():
             qgroup.patch_group_dequant()
     if os.environ.get("SOLUTION_DISABLE_FUSED_HEAD") != "1":
         with installing("fused_head"):
-            from .patches import patch_qwen2_causal_lm
+            from .patches import patch_qwen2_causal_lm, patch_sft_compute_loss
 
             patch_qwen2_causal_lm()
+            try:
+                patch_sft_compute_loss()
+            except ImportError:  # trl absent: the trainer patch is skipped, as the reference does
+                pass
     return sorted(ON)

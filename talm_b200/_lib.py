@@ -25,6 +25,7 @@ SIGNATURES = {
     "talm_last_error": (ctypes.c_char_p, []),
     "talm_status_string": (ctypes.c_char_p, [_INT]),
     "talm_device_status": (_INT, [ctypes.POINTER(_INT)]),
+    "talm_set_wait_limit_ns": (_INT, [ctypes.c_uint64]),
     "talm_profile_begin": (_INT, []),
     "talm_profile_end": (_INT, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_I64), _INT]),
     "talm_nf4_dequantize": (_INT, [_P, _P, _I64, _I64, _P, _P]),

@@ -36,6 +36,14 @@ int current_sm_count() {
   return n;
 }
 
+int current_device(int* dev) {
+  const cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return set_error(TALM_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (*dev < 0 || *dev >= kMaxDevices)
+    return set_error(TALM_ERANGE, "device ordinal %d beyond the library's %d", *dev, kMaxDevices);
+  return TALM_OK;
+}
+
 bool device_is_sm100() {
   int dev = 0, major = 0, minor = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
@@ -52,25 +60,43 @@ struct ProfileRecord {
 };
 static bool g_profile_on = false;
 static std::vector<ProfileRecord> g_profile;
+// Events are reused across profiling sessions: creating two events per launch would add host
+// time to the very loop being timed.
+static std::vector<cudaEvent_t> g_event_pool;
+
+static cudaEvent_t take_event() {
+  if (!g_event_pool.empty()) {
+    cudaEvent_t e = g_event_pool.back();
+    g_event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  return cudaEventCreate(&e) == cudaSuccess ? e : nullptr;
+}
+
+static void give_event(cudaEvent_t e) {
+  if (e != nullptr) g_event_pool.push_back(e);
+}
 
 LaunchTimer::LaunchTimer(int kind, cudaStream_t stream)
     : kind_(kind), stream_(stream), start_(nullptr) {
   if (!g_profile_on) return;
-  cudaEvent_t e;
-  if (cudaEventCreate(&e) == cudaSuccess) {
-    cudaEventRecord(e, stream);
+  cudaEvent_t e = take_event();
+  if (e != nullptr && cudaEventRecord(e, stream) == cudaSuccess) {
     start_ = e;
+  } else {
+    give_event(e);
   }
 }
 
 LaunchTimer::~LaunchTimer() {
   if (start_ == nullptr) return;
-  cudaEvent_t e;
-  if (cudaEventCreate(&e) != cudaSuccess) {
-    cudaEventDestroy(static_cast<cudaEvent_t>(start_));
+  cudaEvent_t e = take_event();
+  if (e == nullptr || cudaEventRecord(e, stream_) != cudaSuccess) {
+    give_event(e);
+    give_event(static_cast<cudaEvent_t>(start_));
     return;
   }
-  cudaEventRecord(e, stream_);
   g_profile.push_back({kind_, static_cast<cudaEvent_t>(start_), e});
 }
 
@@ -156,8 +182,8 @@ const char* talm_status_string(int status) {
 
 int talm_profile_begin(void) {
   for (auto& r : talm::g_profile) {
-    cudaEventDestroy(r.start);
-    cudaEventDestroy(r.stop);
+    talm::give_event(r.start);
+    talm::give_event(r.stop);
   }
   talm::g_profile.clear();
   talm::g_profile_on = true;
@@ -183,8 +209,8 @@ int talm_profile_end(double* ms_out, int64_t* launches_out, int n_kinds) {
       ms_out[r.kind] += ms;
       launches_out[r.kind] += 1;
     }
-    cudaEventDestroy(r.start);
-    cudaEventDestroy(r.stop);
+    talm::give_event(r.start);
+    talm::give_event(r.stop);
   }
   talm::g_profile.clear();
   return status;
@@ -201,6 +227,14 @@ int talm_device_status(int* status_out) {
   if (err != cudaSuccess)
     return talm::set_error(TALM_ECUDA, "device status: %s", cudaGetErrorString(err));
   *status_out = value;
+  return TALM_OK;
+}
+
+int talm_set_wait_limit_ns(uint64_t limit_ns) {
+  const uint64_t value = limit_ns == 0 ? talm::kWaitLimitNs : limit_ns;
+  const cudaError_t err = cudaMemcpyToSymbol(talm::g_wait_limit_ns, &value, sizeof(value));
+  if (err != cudaSuccess)
+    return talm::set_error(TALM_ECUDA, "wait limit: %s", cudaGetErrorString(err));
   return TALM_OK;
 }
 

@@ -20,6 +20,10 @@ int set_error(int status, const char* fmt, ...);
 int check_launch(const char* what);
 int current_sm_count();
 bool device_is_sm100();
+// Per-device caches of the library (kernel attributes, scratch addresses) hold this many
+// devices; current_device() reports an ordinal beyond it as TALM_ERANGE.
+constexpr int kMaxDevices = 64;
+int current_device(int* dev);
 
 // Launch timing (talm_profile_begin / talm_profile_end): a scope around one kernel launch that
 // records CUDA events on the launch stream while profiling is on, and does nothing otherwise.
@@ -58,7 +62,14 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 // Wait limit for every spin in this library: a wait that has not completed after this long
 // records TALM_ETIMEOUT in g_device_status and gives up (the kernel then drains and returns).
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+// The limit of each device lives in g_wait_limit_ns (talm_set_wait_limit_ns changes it, for
+// tests that let a wait run out); each wait reads it once, when it starts to spin.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s, the default
+__device__ uint64_t g_wait_limit_ns = kWaitLimitNs;
+
+__device__ __forceinline__ uint64_t wait_limit_ns() {
+  return *const_cast<const volatile uint64_t*>(&g_wait_limit_ns);
+}
 
 __device__ __forceinline__ void record_timeout() {
   atomicCAS(&g_device_status, 0, TALM_ETIMEOUT);
@@ -105,10 +116,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile int* abort) {
   if (mbar_test(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit_ns();
   while (true) {
     if (mbar_test(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit) {
       *abort = 1;
       record_timeout();
       return false;
@@ -120,8 +132,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
 // already in flight land before shared memory and TMEM are released.
 __device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit_ns();
   while (!mbar_test(bar, parity)) {
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit) {
       record_timeout();
       return false;
     }

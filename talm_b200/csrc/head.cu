@@ -1026,16 +1026,21 @@ Workspace layout(int64_t n_tokens, int64_t n_grad, int64_t vocab_cols, int64_t v
   return w;
 }
 
+// The shared-memory opt-in of a kernel is a property of the kernel on one device: it is set
+// once per device (the current one at the call), under a lock.
 std::mutex g_attr_mutex;
-bool g_attrs_set = false;
+bool g_attrs_set[kMaxDevices] = {};
 
 int set_attrs() {
+  int dev = 0;
+  int st = current_device(&dev);
+  if (st != TALM_OK) return st;
   std::lock_guard<std::mutex> lock(g_attr_mutex);
-  if (g_attrs_set) return TALM_OK;
+  if (g_attrs_set[dev]) return TALM_OK;
   const cudaError_t e = cudaFuncSetAttribute(
       head_slice_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   if (e != cudaSuccess) return set_error(TALM_ECUDA, "smem attribute: %s", cudaGetErrorString(e));
-  g_attrs_set = true;
+  g_attrs_set[dev] = true;
   return TALM_OK;
 }
 

@@ -18,10 +18,11 @@
 // capture begins. Later calls only read the cache.
 //
 // Sharing: every call on a device uses the same scratch, and it keeps what the last call left.
-// The walk writes every scratch byte it reads within the same call and clears the flags that
-// must start at zero (cudaMemsetAsync, as talm_head_shard does), so stale contents never leak
-// into a result. Two calls whose kernels overlap on the GPU (different streams without an
-// ordering between them) race on the scratch: order them, or use talm_head_shard.
+// No scratch state carries from one call to the next: the scratch holds the slice
+// probabilities and the per-part statistics, and a call writes each of them before it reads
+// them; what must start at zero (the caller's stats and acc) is cleared by talm_head_shard
+// itself. Two calls whose kernels overlap on the GPU (different streams without an ordering
+// between them) race on the scratch: order them, or use talm_head_shard.
 //
 // No allocation happens here: no device-memory allocation or release call, no allocating
 // library routine.
@@ -33,7 +34,6 @@ namespace talm {
 namespace head_noalloc {
 
 constexpr size_t kScratchBytes = size_t{16} << 20;  // 16 MiB per device
-constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_head_scratch[kScratchBytes];
 
@@ -43,15 +43,12 @@ static std::mutex g_scratch_mutex;
 // Device address of g_head_scratch on the current device (looked up once per device).
 int scratch_address(void** out) {
   int dev = 0;
-  cudaError_t err = cudaGetDevice(&dev);
-  if (err != cudaSuccess) return set_error(TALM_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(err));
-  if (dev < 0 || dev >= kMaxDevices)
-    return set_error(TALM_ERANGE, "device ordinal %d beyond the %d the scratch table tracks", dev,
-                     kMaxDevices);
+  const int st = current_device(&dev);
+  if (st != TALM_OK) return st;
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
   if (g_scratch_address[dev] == nullptr) {
     void* p = nullptr;
-    err = cudaGetSymbolAddress(&p, g_head_scratch);
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_head_scratch);
     if (err != cudaSuccess || p == nullptr)
       return set_error(TALM_ECUDA, "cudaGetSymbolAddress(scratch) on device %d: %s", dev,
                        cudaGetErrorString(err));

@@ -333,12 +333,9 @@ int64_t run_nf4_tma(const uint8_t* packed, const void* scales, const float* code
                   (reinterpret_cast<uintptr_t>(scales) & 15) == 0;
   if (!ok) return 0;
   // per device: the shared-memory opt-in and the resident CTAs per SM it allows
-  static int per_sm_cache[2][64];
+  static int per_sm_cache[2][kMaxDevices];
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
-    *status = set_error(TALM_ECUDA, "cudaGetDevice failed or ordinal beyond 63");
-    return 0;
-  }
+  if ((*status = current_device(&dev)) != TALM_OK) return 0;
   int per_sm = per_sm_cache[MODE][dev];
   if (per_sm == 0) {
     cudaError_t e = cudaFuncSetAttribute(

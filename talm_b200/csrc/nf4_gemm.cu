@@ -118,10 +118,11 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
                                                   volatile int* abort) {
   if (mbar_test_cluster(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit_ns();
   while (true) {
     if (mbar_test_cluster(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit) {
       *abort = 1;
       record_timeout();
       return false;
@@ -393,19 +394,23 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) tmem_dealloc_pair(tmem_base, TMEM_COLS);
 }
 
+// Shared-memory opt-in of both kernel variants, once per device (see head.cu's set_attrs).
 std::mutex g_attr_mutex;
-bool g_attrs_set = false;
+bool g_attrs_set[kMaxDevices] = {};
 
 int set_attrs() {
+  int dev = 0;
+  int st = current_device(&dev);
+  if (st != TALM_OK) return st;
   std::lock_guard<std::mutex> lock(g_attr_mutex);
-  if (g_attrs_set) return TALM_OK;
+  if (g_attrs_set[dev]) return TALM_OK;
   cudaError_t e = cudaFuncSetAttribute(nf4_gemm_kernel<false>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(nf4_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              SMEM_BYTES);
   if (e != cudaSuccess) return set_error(TALM_ECUDA, "smem attribute: %s", cudaGetErrorString(e));
-  g_attrs_set = true;
+  g_attrs_set[dev] = true;
   return TALM_OK;
 }
 

@@ -23,9 +23,9 @@
 //
 // A phase ends when the last CTA of the writing kernel (a device-scope counter) raises the
 // phase flag of its rank on every rank, after every CTA fenced its stores at system scope. A
-// waiting CTA polls its own flags with acquire loads; every wait is bounded (kWaitLimitNs) and
-// records TALM_ETIMEOUT on expiry, after which the kernel returns without its work. Data that
-// other GPUs write while a kernel runs is read with L2-only loads (__ldcg).
+// waiting CTA polls its own flags with acquire loads; every wait is bounded (g_wait_limit_ns,
+// 2 s by default) and records TALM_ETIMEOUT on expiry, after which the kernel returns without
+// its work. Data that other GPUs write while a kernel runs is read with L2-only loads (__ldcg).
 #include <string.h>
 
 #include "common.cuh"
@@ -77,10 +77,11 @@ __device__ bool cta_wait_phase(const uint8_t* own, size_t flags_off, int phase, 
   if (threadIdx.x == 0) {
     const uint32_t* f = reinterpret_cast<const uint32_t*>(own + flags_off) + phase * world;
     const uint64_t t0 = globaltimer_ns();
+    const uint64_t limit = wait_limit_ns();
     int good = 1;
     for (int q = 0; q < world && good; ++q) {
       while (static_cast<int32_t>(ld_acquire_sys(f + q) - epoch) < 0) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (globaltimer_ns() - t0 > limit) {
           record_timeout();
           good = 0;
           break;

@@ -18,6 +18,12 @@ accumulator tiles (softmax(z) W over the labelled rows) of slice s-1 -- each fol
 per-row merge launch. The host code here keeps the reference's contract around it: the
 labelled-first row order (`labelled_first`; `labelled_first_rows` is the same order built on
 the device), the denominator, the autograd Function and the module switches.
+
+That host code restates otarernazar-eng/Talm's solution/fused_head.py (Apache License 2.0,
+"Soup Kernel Challenge starter kit", Copyright 2026 Makazhan Alpamys and the Soup contributors):
+`labelled_first`, `_denominator`, `_head_backward`'s expression, the autograd contract and the
+`fused_head_loss` dispatch follow that file, because callers and tests depend on them; the
+kernels are this package's own.
 """
 
 import os

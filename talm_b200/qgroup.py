@@ -12,6 +12,13 @@ reference's host logic (qgroup.py:194-328), restated here; only the kernel diffe
 
 Failures: the reference answers an unexpected error with bitsandbytes' own dequantization. Here
 the error is recorded (state.fallback) and raised: there is no second implementation.
+
+The host logic restates otarernazar-eng/Talm's solution/qgroup.py (Apache License 2.0, "Soup
+Kernel Challenge starter kit", Copyright 2026 Makazhan Alpamys and the Soup contributors): the
+packing of the seven projections (`LayerGroup.__init__`), the per-pass cache and its use
+counting (`reset` ... `span_bias`), `GroupLinear`, the level table and the layer / Linear4bit
+patches follow that file statement for statement, because callers and tests depend on their
+exact behaviour; the CUDA kernels they call are this package's own.
 """
 
 import os

@@ -322,3 +322,38 @@ def test_device_labelled_first_matches_reference_order(n, frac):
     assert torch.equal(src, ref_src)
     assert torch.equal(rows, hidden.index_select(0, ref_src))
     assert torch.equal(rows_targets, targets.index_select(0, ref_src))
+
+
+def test_token_chunked_entry_point_matches_the_vocab_path():
+    """solution/test_kernels.py:285-330: `token_chunk=` selects FusedHeadLoss (the reference's
+    token-chunked path, routed here to the same sm_100a walk) - the same loss, per-token loss,
+    entropy and accuracy as the vocabulary-sliced entry point, both against the reference's
+    formulas, with confident rows among ordinary ones; the dispatch counters move as the
+    reference's do (fused_head.py:447-462)."""
+    from talm_b200.engaged import FELL_BACK, RAN
+    from talm_b200.fused_head import fused_head_loss
+
+    torch.manual_seed(11)
+    n, size, vocab = 700, 1536, 151936
+    weight = (torch.randn(vocab, size, device=DEV) * 0.03).half()
+    targets = torch.randint(0, vocab, (n,), device=DEV)
+    targets[torch.rand(n, device=DEV) < 0.35] = -100
+    hidden = torch.randn(n, size, device=DEV, dtype=torch.float16) * 1.5
+    confident = (torch.rand(n, device=DEV) < 0.3) & (targets >= 0)
+    hidden[confident] = (weight[targets[confident]].float() * 400).half()
+    outs = {}
+    for path, kw in (("tokens", {"token_chunk": 256}), ("vocab", {})):
+        ran, fell = RAN["vchunk"], FELL_BACK["vchunk"]
+        x = hidden.clone().requires_grad_(True)
+        loss, token_loss, entropy, correct = fused_head_loss(x, weight, targets, None, **kw)
+        (loss * 1024.0).backward()
+        outs[path] = (loss.detach(), token_loss, entropy, correct, x.grad)
+        if path == "tokens":
+            assert (RAN["vchunk"], FELL_BACK["vchunk"]) == (ran, fell + 1)
+        else:
+            assert (RAN["vchunk"], FELL_BACK["vchunk"]) == (ran + 1, fell)
+    for a, b in zip(outs["tokens"], outs["vocab"]):
+        assert torch.equal(a, b)
+    ref = gpu_reference(hidden, weight, targets, grad_scale=1024.0)
+    check_head(outs["tokens"][:4], ref, outs["tokens"][4], "token_chunk=256")
+    assert (outs["tokens"][4][targets < 0] == 0).all()

@@ -19,11 +19,11 @@ DEV = "cuda"
 SCRATCH_BYTES = 16 << 20
 
 
-def _case(seed, n, vocab, size):
-    g = torch.Generator(device=DEV).manual_seed(seed)
-    hidden = torch.randn(n, size, generator=g, device=DEV).half()
-    weight = (torch.randn(vocab, size, generator=g, device=DEV) * 0.05).half()
-    targets = torch.randint(0, vocab, (n,), generator=g, device=DEV)
+def _case(seed, n, vocab, size, dev=DEV):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    hidden = torch.randn(n, size, generator=g, device=dev).half()
+    weight = (torch.randn(vocab, size, generator=g, device=dev) * 0.05).half()
+    targets = torch.randint(0, vocab, (n,), generator=g, device=dev)
     # a row whose maximum jumps in a later slice, so the rescaling path runs too
     hidden[3] = (weight[vocab - 5].float() * 30).half()
     targets[3] = vocab - 5
@@ -33,12 +33,13 @@ def _case(seed, n, vocab, size):
 def _with_workspace(lib, hidden, weight, targets, n_grad, chunk):
     n, size = hidden.shape
     vocab = weight.shape[0]
-    stats = torch.full((n, _lib.HEAD_STATS), float("nan"), device=DEV)
-    acc = torch.full((n_grad, size), float("nan"), device=DEV)
+    dev = hidden.device
+    stats = torch.full((n, _lib.HEAD_STATS), float("nan"), device=dev)
+    acc = torch.full((n_grad, size), float("nan"), device=dev)
     need = ctypes.c_size_t(0)
     _lib.check(lib.talm_head_workspace_size(n, n_grad, size, vocab, chunk, ctypes.byref(need)),
                "talm_head_workspace_size")
-    ws = torch.empty(need.value, dtype=torch.uint8, device=DEV)
+    ws = torch.empty(need.value, dtype=torch.uint8, device=dev)
     _lib.check(lib.talm_head_shard(hidden.data_ptr(), size, weight.data_ptr(), size,
                                    targets.data_ptr(), n, n_grad, size, vocab, 0, chunk,
                                    stats.data_ptr(), acc.data_ptr(), ws.data_ptr(), need.value,
@@ -49,8 +50,9 @@ def _with_workspace(lib, hidden, weight, targets, n_grad, chunk):
 def _without_workspace(lib, hidden, weight, targets, n_grad, chunk):
     n, size = hidden.shape
     vocab = weight.shape[0]
-    stats = torch.full((n, _lib.HEAD_STATS), float("nan"), device=DEV)
-    acc = torch.full((n_grad, size), float("nan"), device=DEV)
+    dev = hidden.device
+    stats = torch.full((n, _lib.HEAD_STATS), float("nan"), device=dev)
+    acc = torch.full((n_grad, size), float("nan"), device=dev)
     _lib.check(lib.talm_head_shard_noalloc(hidden.data_ptr(), size, weight.data_ptr(), size,
                                            targets.data_ptr(), n, n_grad, size, vocab, 0, chunk,
                                            stats.data_ptr(), acc.data_ptr(),
@@ -69,15 +71,32 @@ def test_no_alloc_matches_the_workspace_entry_point_on_consecutive_calls():
         ref_stats, ref_acc = _with_workspace(lib, hidden, weight, targets, n_grad, chunk)
         stats, acc = _without_workspace(lib, hidden, weight, targets, n_grad, chunk)
         torch.cuda.synchronize()
-        for field in (_lib.STAT_M, _lib.STAT_S, _lib.STAT_T, _lib.STAT_ZT, _lib.STAT_BEST,
-                      _lib.STAT_HIT, 7):
-            torch.testing.assert_close(stats[:, field], ref_stats[:, field], rtol=1e-5,
-                                       atol=1e-6)
-        assert torch.equal(stats[:, _lib.STAT_IDX].view(torch.int32),
-                           ref_stats[:, _lib.STAT_IDX].view(torch.int32))
-        torch.testing.assert_close(acc, ref_acc, rtol=1e-3,
-                                   atol=float(ref_acc.abs().max()) * 2 ** -10)
+        _same_bits(stats, ref_stats, acc, ref_acc)
     assert _lib.device_status() == 0
+
+
+def _same_bits(stats, ref_stats, acc, ref_acc):
+    # both entry points run the same whole-tile kernels, which add every accumulator element
+    # in the same order on every call: the results are the same bits
+    assert torch.equal(stats.view(torch.int32), ref_stats.view(torch.int32))
+    assert torch.equal(acc.view(torch.int32), ref_acc.view(torch.int32))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_both_entry_points_on_two_devices_in_one_process():
+    # the shared-memory opt-in of the slice kernel and the scratch address are per device: a
+    # process that drives two GPUs must get a working launch and its own scratch on each
+    lib = _lib.load()
+    for index in (0, 1, 0):
+        dev = torch.device("cuda", index)
+        with torch.cuda.device(dev):
+            hidden, weight, targets = _case(30 + index, 260, 3000, 256, dev)
+            ref_stats, ref_acc = _with_workspace(lib, hidden, weight, targets, 200, 1024)
+            stats, acc = _without_workspace(lib, hidden, weight, targets, 200, 1024)
+            torch.cuda.synchronize(dev)
+            _same_bits(stats, ref_stats, acc, ref_acc)
+            assert _lib.device_status() == 0
 
 
 def test_no_alloc_refuses_work_beyond_its_scratch():
