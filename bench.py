@@ -507,18 +507,30 @@ def run_head(world, rank, local, steps, warmup, hidden, weight, targets, clocks_
 
 
 def run_head_e2e(world, rank, steps, warmup, hidden, weight, targets):
-    """Public API with host buffers: H2D of the step's hidden states + labels, D2H of the loss."""
+    """Public API with host buffers: H2D of the step's hidden states + labels, D2H of the loss.
+    At N > 1 each rank copies its 1/N of the hidden rows from pinned host memory and the ranks
+    all-gather them over NVLink (NCCL), instead of N full host copies; the labels (8 B a row)
+    are copied whole by every rank."""
     from talm_b200.fused_head import fused_head_loss
     from talm_b200.vocab_parallel import shard_bounds, vocab_parallel_head_loss
 
-    h_host = hidden.cpu().pin_memory()
+    n = hidden.shape[0]
+    r0, nr = shard_bounds(n, world, rank) if world > 1 else (0, n)
+    equal = world > 1 and n % world == 0
+    h_host = (hidden[r0:r0 + nr] if equal else hidden).cpu().pin_memory()
     t_host = targets.cpu().pin_memory()
     n_lab = int((t_host >= 0).sum())
     col0 = shard_bounds(VOCAB, world, rank)[0] if world > 1 else 0
+    full = torch.empty_like(hidden) if equal else None
     sink = []
 
     def step():
-        h = h_host.to("cuda", non_blocking=True).requires_grad_(True)
+        part = h_host.to("cuda", non_blocking=True)
+        if equal:
+            dist.all_gather_into_tensor(full, part)
+            h = full.detach().requires_grad_(True)
+        else:
+            h = part.requires_grad_(True)
         t = t_host.to("cuda", non_blocking=True)
         if world == 1:
             loss, *_ = fused_head_loss(h, weight, t, None, CHUNK, n_labelled=n_lab)
@@ -531,7 +543,7 @@ def run_head_e2e(world, rank, steps, warmup, hidden, weight, targets):
     for _ in range(warmup):
         step()
     ms = timed(step, steps, world)
-    h2d = (h_host.numel() * h_host.element_size() + t_host.numel() * 8) * world
+    h2d = h_host.numel() * h_host.element_size() * world + t_host.numel() * 8 * world
     return ms / steps, h2d, 4 * world
 
 
@@ -563,9 +575,12 @@ def run_nf4(world, rank, steps, warmup, n_layers=N_LAYERS):
                              "grouped launch per layer, layers sharded contiguously over the ranks",
                  "GB_per_s": total_bytes / (ms / steps) / 1e6, "ms_per_sweep": ms / steps,
                  "bytes_per_sweep": total_bytes,
-                 "kernel_us_per_layer": 1000 * k_ms / max(k_n, 1),
-                 "kernel_us_source": "a second pass of the same sweep with one CUDA event pair "
-                                     "per launch (the timed region itself has none)"}
+                 "us_per_layer": 1000 * ms / steps / max(nl, 1),
+                 "us_per_layer_source": "the timed region (launches back to back, each starting "
+                                        "its set-up under the previous one's tail) / its launches",
+                 "kernel_us_per_layer_events": 1000 * k_ms / max(k_n, 1),
+                 "events_note": "a second pass with one CUDA event pair per launch: the events "
+                                "serialise the launches, so this includes the launch gaps"}
     del layers
     if world == 1:
         # config 1: fp32 absmax, one launch per layer over its concatenated buffers; eight
@@ -608,17 +623,20 @@ def parity_check(world, rank, hidden, weight_full, weight, targets, col0):
     from talm_b200.fused_head import fused_head_loss
     from talm_b200.vocab_parallel import vocab_parallel_head_loss
 
-    def run(fn, h, *a, **k):
+    def run(fn, h, t, *a, **k):
+        # backward of loss * (labelled rows): the mean's 1/denominator cancels, so the compared
+        # gradient is the head's dH itself (rounded to fp16 once) instead of values scaled
+        # into fp16's subnormal range
         x = h.detach().clone().requires_grad_(True)
-        out = fn(x, *a, **k)
-        out[0].backward()
-        return [t.detach() for t in out], x.grad
+        out = fn(x, *a[:1], t, *a[1:], **k)
+        (out[0] * float(max(int((t >= 0).sum()), 1))).backward()
+        return [v.detach() for v in out], x.grad
 
     if world > 1:
         n_lab = int((targets >= 0).sum())
-        got, g = run(vocab_parallel_head_loss, hidden, weight, targets, VOCAB, col0, None, CHUNK,
-                     n_labelled=n_lab)
-        ref, rg = run(fused_head_loss, hidden, weight_full, targets, None, CHUNK,
+        got, g = run(vocab_parallel_head_loss, hidden, targets, weight, VOCAB, col0, None,
+                     CHUNK, n_labelled=n_lab)
+        ref, rg = run(fused_head_loss, hidden, targets, weight_full, None, CHUNK,
                       n_labelled=n_lab)
         tol = (1e-5, 1e-5)
         what = "vocab-parallel head vs the single-GPU head on the full weight, all rows"
@@ -626,8 +644,10 @@ def parity_check(world, rank, hidden, weight_full, weight, targets, col0):
         from oracle.head import reference_head
 
         rows = 64
-        got, g = run(fused_head_loss, hidden[:rows], weight, targets[:rows], None, CHUNK)
-        r = reference_head(hidden[:rows].cpu(), weight.cpu(), targets[:rows].cpu())
+        got, g = run(fused_head_loss, hidden[:rows], targets[:rows], weight, None, CHUNK)
+        n_lab = max(int((targets[:rows] >= 0).sum()), 1)
+        r = reference_head(hidden[:rows].cpu(), weight.cpu(), targets[:rows].cpu(),
+                           grad_scale=float(n_lab))
         ref = [t.to(hidden.device) for t in r[:4]]
         rg = r[4].to(hidden.device)
         tol = (1e-4, 1e-4)
@@ -787,6 +807,10 @@ def ours(args, world, rank, local):
                                                      "still in L2, so its DRAM bytes understate "
                                                      "the launch's traffic"}
         nf4["c3"]["frac_of_hbm_per_gpu"] = nf4["c3"]["GB_per_s"] / world / pk["hbm_gbs"]
+        nf4["c3"]["roofline"] = {"bound": "hbm", "achieved": nf4["c3"]["GB_per_s"] / world,
+                                 "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                 "frac": nf4["c3"]["GB_per_s"] / world / pk["hbm_gbs"],
+                                 "traffic": None}
         line["nf4"] = nf4
         if world == 1 and rank == 0:
             line["cpu_baseline"] = cpu_head_baseline(weight, c4_inputs("cuda")[0],

@@ -53,6 +53,11 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 __device__ __forceinline__ void grid_dependency_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
+// Lets the next kernel of the stream (launched with programmatic stream serialization) start
+// its set-up now; it still waits in grid_dependency_wait until this grid has completed.
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
@@ -343,6 +348,13 @@ __device__ __forceinline__ uint32_t ld_stream_u32(const uint32_t* p) {
 
 __device__ __forceinline__ void st_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+// 16-byte store marked streaming (evict-first in L2): output that this kernel never reads back
+__device__ __forceinline__ void st_v4_stream(void* p, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.global.cs.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c),
                "r"(d)
                : "memory");
 }

@@ -154,6 +154,14 @@ __global__ void __launch_bounds__(256) nf4_bytes_kernel(const uint8_t* __restric
 // with coalesced 16-byte stores (512 contiguous bytes per warp instruction), which need no
 // wait. Scale modes: 0 = fp32 absmax per block, 1 = double-quantised.
 // ------------------------------------------------------------------------------------------
+// Output stores of the bulk kernel: streaming (evict-first) by default.
+#ifndef NF4_STORE
+#define NF4_STORE st_v4_stream
+#endif
+// The bulk kernel is launched with programmatic stream serialization (1) unless built with 0.
+#ifndef NF4_PDL
+#define NF4_PDL 1
+#endif
 constexpr int kTileBytes = 8192;          // packed bytes per tile
 constexpr int kTmaStages = 4;
 constexpr int kScaleBytes = 1024;         // room for a tile's scales (fp32 at blocksize 64)
@@ -215,6 +223,13 @@ __global__ void __launch_bounds__(kNf4TmaThreads) nf4_tma_kernel(
     abort_flag = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
+  }
+  // Launched with programmatic stream serialization: everything above overlapped the previous
+  // kernel's tail; every read of an input and every write of the output comes after it has
+  // completed. The next layer's launch may then start its own set-up at once.
+  grid_dependency_wait();
+  grid_launch_dependents();
+  if (tid == producer) {
     // The first pass over the ring needs no wait for a free slot: with only the 64-byte level
     // table to fill, start it at once. The double-quantised path first fills its 1 KiB code
     // table, which every CTA reads from the same addresses; a burst of tile loads queued ahead
@@ -305,7 +320,7 @@ __global__ void __launch_bounds__(kNf4TmaThreads) nf4_tma_kernel(
       const uint32_t p1 = nf4_pair(lut, (w >> 8) & 0xffu, sc[k]);
       const uint32_t p2 = nf4_pair(lut, (w >> 16) & 0xffu, sc[k]);
       const uint32_t p3 = nf4_pair(lut, w >> 24, sc[k]);
-      st_v4(out4 + (byte >> 2), p0, p1, p2, p3);
+      NF4_STORE(out4 + (byte >> 2), p0, p1, p2, p3);
     }
     if (++stage == kTmaStages) { stage = 0; phase ^= 1; }
   }
@@ -359,9 +374,19 @@ int64_t run_nf4_tma(const uint8_t* packed, const void* scales, const float* code
                            : -1;
   {
     LaunchTimer timer(TALM_KERNEL_NF4, stream);
-    nf4_tma_kernel<MODE><<<grid, kNf4TmaThreads, kNf4TmaSmem, stream>>>(
-        packed, scales, code, absmax2, offset2, qblock2, q2_shift,
-        reinterpret_cast<uint32_t*>(out), n_tiles, shift, levels);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.blockDim = dim3(kNf4TmaThreads, 1, 1);
+    cfg.dynamicSmemBytes = kNf4TmaSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = NF4_PDL;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, nf4_tma_kernel<MODE>, packed, scales, code, absmax2, offset2,
+                       qblock2, q2_shift, reinterpret_cast<uint32_t*>(out), n_tiles, shift,
+                       levels);
   }
   *status = check_launch("nf4 bulk kernel");
   return *status == TALM_OK ? n_tiles * kTileBytes : 0;
