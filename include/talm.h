@@ -178,14 +178,6 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
                     int64_t vocab_chunk, float* stats, float* acc, void* workspace,
                     size_t ws_bytes, void* stream);
 
-/* Caps the SMs that the slice kernels of later talm_head_shard calls on the current device may
- * occupy (rounded down to whole CTA pairs); 0 restores the default, every SM. Host-side state
- * read when a call launches. For a caller that runs other kernels beside the walk on a second
- * stream (the vocabulary-parallel exchange of an earlier token block), so that those kernels
- * find free SMs instead of waiting for the slice kernel's persistent grid to finish. No
- * reference counterpart (the reference runs one stream). */
-int talm_head_set_sm_budget(int64_t sms);
-
 /* talm_head_shard with no workspace argument, for callers that cannot allocate device memory
  * where they call the head (a fixed memory plan that must not grow, an allocator owned by
  * another runtime, a C caller with no allocator binding). No counterpart in the reference: its

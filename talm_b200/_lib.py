@@ -35,7 +35,6 @@ SIGNATURES = {
     "talm_head_workspace_size": (_INT, [_I64, _I64, _I64, _I64, _I64, ctypes.POINTER(_SZ)]),
     "talm_head_shard": (_INT, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P,
                                _P, _P, _SZ, _P]),
-    "talm_head_set_sm_budget": (_INT, [_I64]),
     "talm_head_shard_noalloc": (_INT, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64,
                                        _I64, _P, _P, _P]),
     "talm_head_finalize": (_INT, [_P, _P, _I64, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _P,

@@ -774,7 +774,16 @@ __global__ void __launch_bounds__(256) head_finalize_kernel(
     float* __restrict__ token_entropy, int* __restrict__ correct, GradDest dest, int vec4,
     peer::PeerLayout L, int world, uint32_t epoch) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * 8 + warp;
+  // Under the peer exchange the gradient rows go to their owners: rows [q * rpr, +rpr) to rank
+  // q. CTAs start roughly in index order, so every rank walking the rows from 0 would send to
+  // rank 0 first, then rank 1, ... (all ranks into one receiver at a time). Rank r starts its
+  // walk at the rows of rank r + 1 instead: at any moment the ranks send to different owners.
+  int block = blockIdx.x;
+  if (dest.peers != nullptr && world > 1) {
+    const long long first = (static_cast<long long>((dest.rank + 1) % world) * dest.rpr) / 8;
+    block = static_cast<int>((block + first) % gridDim.x);
+  }
+  const int row = block * 8 + warp;
   if (row < n_tokens)
     finalize_row(row, lane, stats, targets, n_grad, acc, acc_scale, weight, ld_weight, col0,
                  vcols, hidden, grad_rows, token_loss, token_entropy, correct, dest, vec4);
@@ -1076,30 +1085,11 @@ int launch_slice_step(const CUtensorMap& tm_hidden, const CUtensorMap& tm_weight
 // Pairs that fit on the GPU at once (one CTA per SM: shared memory and TMEM are taken whole).
 int max_pairs_of(int sms) { return sms / 2 > 0 ? sms / 2 : 1; }
 
-// SM budget of the slice kernel per device (talm_head_set_sm_budget; 0 = every SM).
-int g_sm_budget[kMaxDevices] = {};
-
-int slice_sms(int sms) {
-  int dev = 0;
-  if (current_device(&dev) != TALM_OK) return sms;
-  const int budget = g_sm_budget[dev];
-  return budget > 0 && budget < sms ? budget : sms;
-}
 
 }  // namespace head
 }  // namespace talm
 
 extern "C" {
-
-int talm_head_set_sm_budget(int64_t sms) {
-  using namespace talm;
-  if (sms < 0) return set_error(TALM_EINVAL, "the SM budget cannot be negative");
-  int dev = 0;
-  const int st = current_device(&dev);
-  if (st != TALM_OK) return st;
-  head::g_sm_budget[dev] = static_cast<int>(sms > (1 << 20) ? (1 << 20) : sms);
-  return TALM_OK;
-}
 
 int talm_head_workspace_size(int64_t n_tokens, int64_t n_grad, int64_t hidden,
                              int64_t vocab_cols, int64_t vocab_chunk, size_t* bytes) {
@@ -1165,7 +1155,7 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
 
   const int k_blocks = static_cast<int>((hidden_size + BK - 1) / BK);
   const int n_pair_rows = static_cast<int>((n_tokens + PAIR_ROWS - 1) / PAIR_ROWS);
-  const int max_pairs = max_pairs_of(slice_sms(sms));
+  const int max_pairs = max_pairs_of(sms);
   // Step k runs the logits GEMM of slice k (k < n_slices) together with the accumulator GEMM
   // of slice k - 1 (k >= 1), then the combine of slice k. The slices' probability buffers
   // alternate: step k writes buffer k % 2 while its accumulator part reads buffer (k - 1) % 2.

@@ -125,8 +125,10 @@ __global__ void __launch_bounds__(256) publish_stats_kernel(const float4* __rest
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
        i += stride) {
     const float4 v = stats[i];
-    for (int q = 0; q < world; ++q)
+    for (int k = 1; k <= world; ++k) {  // ranks after this one first: no common first receiver
+      const int q = (rank + k) % world;
       reinterpret_cast<float4*>(peers[q] + L.stats)[rank * n4 + i] = v;
+    }
   }
   cta_signal_phase(own, peers, L.flags, L.counters, 0, rank, world, epoch);
 }
@@ -158,8 +160,10 @@ __global__ void __launch_bounds__(256) reduce_gather_kernel(const unsigned long 
     const uint4 h = make_uint4(pack_half2(a[0], a[1]), pack_half2(a[2], a[3]),
                                pack_half2(a[4], a[5]), pack_half2(a[6], a[7]));
     const long long o = (row0 + j) * hidden + c;
-    for (int q = 0; q < world; ++q)
+    for (int k = 1; k <= world; ++k) {  // ranks after this one first: no common first receiver
+      const int q = (rank + k) % world;
       *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(peers[q] + L.dh) + o) = h;
+    }
   }
   cta_signal_phase(own, peers, L.flags, L.counters, 2, rank, world, epoch);
 }

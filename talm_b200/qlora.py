@@ -12,10 +12,14 @@ The reference's step plugs the same two paths into the same model (solution/patc
 for the head call, solution/qgroup.py:474-545 for the layer hooks, solution/lora.py:151-231 for
 the adapter arithmetic).
 
-What the reference's step has that this one does not: PEFT and trl around the model, the varlen
-packing of the batch (solution/unpad.py; here the padded batch runs with an attention mask and
-the head skips the -100 rows), a gradient scaler for fp16 training (here the frozen model is
-fp16 and the adapters fp32, with no loss scaling), and gradient checkpointing.
+Padding removal (solution/unpad.py) comes in two forms: `varlen_train_step` gathers the real
+tokens on the device after one host read of the row lengths (`unpad_batch`, as the reference
+does) and runs attention in PyTorch's variable-length mode over the packed rows
+(`varlen_attention`); `pack_batch` builds the same packed tokens on the host before upload, for
+the CUDA-graph replay (`GraphedStep.packed`, a block-causal mask). What the reference's step has
+that this one does not: PEFT and trl around the model, a gradient scaler for fp16 training (here
+the frozen model is fp16 and the adapters fp32, with no loss scaling), and gradient
+checkpointing.
 """
 
 import math
@@ -283,6 +287,101 @@ def pack_batch(batch, device, bucket=256):
     out = {k: v.to(device, non_blocking=True) for k, v in packed.items()}
     out.update(n_real=n_real, n_labelled=n_labelled)
     return out
+
+
+def unpad_batch(batch, bucket=0):
+    """Padding removal on the device (solution/unpad.py:66-95): the real tokens of a right-padded
+    DEVICE batch packed row after row into one sequence, with one host read (the row lengths and
+    the labelled count, in a single copy). Returns input_ids [1, T], position_ids [1, T] (each
+    token's position in its row), targets [T] (the padded batch's shifted labels at the kept
+    positions), cu_seqlens int32 [rows + 1] (row bounds in the packed sequence; with `bucket`,
+    T is rounded up to a multiple of it and one more bound closes a filler segment of id-0
+    tokens with target -100), max_len (the longest segment) and the host counts n_real and
+    n_labelled."""
+    ids, mask, labels = batch["input_ids"], batch["attention_mask"], batch["labels"]
+    rows, seq = ids.shape
+    device = ids.device
+    lengths_dev = mask.to(torch.int64).sum(1)
+    shift = F.pad(labels, (0, 1), value=-100)[:, 1:]
+    inside = torch.arange(seq, device=device)[None] < lengths_dev[:, None]
+    n_lab_dev = ((shift >= 0) & inside).sum()
+    values = torch.cat((lengths_dev, n_lab_dev[None])).tolist()  # the one host read
+    lengths, n_labelled = [int(v) for v in values[:rows]], int(values[rows])
+    n_real = sum(lengths)
+    total = -(-n_real // bucket) * bucket if bucket else n_real
+    fill = total - n_real
+    idx = torch.cat([torch.arange(n, device=device) + b * seq for b, n in enumerate(lengths)])
+    pos = torch.cat([torch.arange(n, device=device) for n in lengths]
+                    + ([torch.arange(fill, device=device)] if fill else []))
+    flat_ids, flat_tgt = ids.reshape(-1)[idx], shift.reshape(-1)[idx]
+    if fill:
+        flat_ids = torch.cat([flat_ids, flat_ids.new_zeros(fill)])
+        flat_tgt = torch.cat([flat_tgt, flat_tgt.new_full((fill,), -100)])
+    bounds = [0]
+    for n in lengths:
+        bounds.append(bounds[-1] + n)
+    if fill:
+        bounds.append(total)
+    cu = torch.tensor(bounds, dtype=torch.int32).to(device, non_blocking=True)
+    max_len = max([b - a for a, b in zip(bounds[:-1], bounds[1:])] + [1])
+    return {"input_ids": flat_ids[None], "position_ids": pos[None], "targets": flat_tgt,
+            "cu_seqlens": cu, "max_len": max_len, "n_real": n_real, "n_labelled": n_labelled}
+
+
+VARLEN = "talm_varlen"
+
+
+def varlen_attention(module, query, key, value, attention_mask, scaling=None, dropout=0.0,
+                     **kwargs):
+    """Causal attention over a packed sequence whose segments are given by `cu_seq_lens_q` /
+    `max_length_q` (transformers passes the model's keyword arguments through), in one call of
+    PyTorch's variable-length flash-attention kernel: no [T, T] mask, no attention across
+    segments, grouped key/value heads used as they are. The reference runs the
+    memory-efficient kernel's variable-length mode for the same purpose
+    (solution/unpad.py:199-295). query [1, Hq, T, D], key/value [1, Hkv, T, D] -> [1, T, Hq, D]."""
+    from torch.nn.attention.varlen import varlen_attn
+
+    if dropout:
+        raise ValueError("the packed attention path has no attention dropout")
+    cu, max_len = kwargs["cu_seq_lens_q"], int(kwargs["max_length_q"])
+    q = query[0].transpose(0, 1)
+    k = key[0].transpose(0, 1)
+    v = value[0].transpose(0, 1)
+    out = varlen_attn(q, k, v, cu, cu, max_len, max_len, scale=scaling, window_size=(-1, 0))
+    return out[None], None
+
+
+def _register_varlen():
+    from transformers import AttentionInterface
+
+    AttentionInterface.register(VARLEN, varlen_attention)
+
+
+def _varlen_hidden(model, packed):
+    """The decoder over a packed batch (`unpad_batch`) with the variable-length attention."""
+    _register_varlen()
+    config = model.config
+    previous = config._attn_implementation
+    config._attn_implementation = VARLEN
+    try:
+        cu = packed["cu_seqlens"]
+        return model.model(input_ids=packed["input_ids"], position_ids=packed["position_ids"],
+                           cu_seq_lens_q=cu, cu_seq_lens_k=cu, max_length_q=packed["max_len"],
+                           max_length_k=packed["max_len"], use_cache=False).last_hidden_state
+    finally:
+        config._attn_implementation = previous
+
+
+def varlen_train_step(model, optimizer, batch, bucket=0):
+    """The training step with the padding removed on the device (`unpad_batch`: one host read)
+    and variable-length attention over the packed rows; the fused head over the kept tokens'
+    targets, backward, one optimizer step."""
+    packed = unpad_batch(batch, bucket)
+    loss = _packed_loss(model, _varlen_hidden(model, packed), packed)
+    loss.backward()
+    optimizer.step()
+    optimizer.zero_grad(set_to_none=True)
+    return loss.detach()
 
 
 def block_causal_mask(segments):

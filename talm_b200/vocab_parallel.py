@@ -96,14 +96,6 @@ class CudaHeadOps:
 OPS = CudaHeadOps()
 
 PEER_EXCHANGE = os.environ.get("TALM_B200_PEER_EXCHANGE", "1") != "0"
-# The peer flow walks the rows in two token blocks: while the second block walks the
-# vocabulary, the first block's exchange runs on a second stream on SMs the walk leaves free
-# (talm_head_set_sm_budget). SPLIT = share of the rows in the first block (0 or 1: one block);
-# EXCHANGE_SMS = SMs left to the exchange; calls with fewer than 2 * SPLIT_MIN_ROWS rows walk
-# in one block.
-SPLIT = float(os.environ.get("TALM_B200_EXCHANGE_SPLIT", "0"))
-EXCHANGE_SMS = int(os.environ.get("TALM_B200_EXCHANGE_SMS", "16"))
-SPLIT_MIN_ROWS = 1024
 
 
 class PeerExchange:
@@ -178,42 +170,19 @@ class PeerExchange:
 
 
 _EXCHANGES = {}
-_SIDE_STREAMS = {}
 
 
-def _exchange(group, device, n_tokens, hidden_cols, block=0):
-    """The peer exchange of token block `block` (each block has its own buffer and epochs, so
-    the two blocks' exchanges can be in flight at once)."""
-    key = (id(group) if group is not None else None, device.index, block)
+def _exchange(group, device, n_tokens, hidden_cols):
+    key = (id(group) if group is not None else None, device.index)
     ex = _EXCHANGES.get(key)
     if ex is None:
         ex = _EXCHANGES[key] = PeerExchange(group, device)
     return ex if ex.ensure(n_tokens, hidden_cols) else None
 
 
-def _side_stream(device):
-    s = _SIDE_STREAMS.get(device.index)
-    if s is None:
-        s = _SIDE_STREAMS[device.index] = torch.cuda.Stream(device)
-    return s
-
-
-def token_blocks(n_tokens):
-    """[(first, end)) row ranges of the peer flow's token blocks: the same on every rank (they
-    depend only on the replicated row count). The first block holds about SPLIT of the rows,
-    rounded to whole CTA-pair row blocks (256 rows) where the minimum block size allows."""
-    if not 0.0 < SPLIT < 1.0 or n_tokens < 2 * SPLIT_MIN_ROWS:
-        return [(0, n_tokens)]
-    first = int(round(n_tokens * SPLIT / 256.0)) * 256
-    first = min(max(first, SPLIT_MIN_ROWS), n_tokens - SPLIT_MIN_ROWS)
-    return [(0, first), (first, n_tokens)]
-
-
-def _peer_block(ex, stats, acc, rows_targets, n_grad, w16, ld_w, col0, cols, need_grad,
-                token_loss, token_entropy, correct, grad):
-    """Steps 2-5 of one token block through the peer buffers, on the current stream, writing
-    the block's per-row outputs and (need_grad) its reduced fp16 gradient rows into the given
-    tensors, in the block's row order."""
+def _peer_flow(ex, stats, acc, rows_targets, n_grad, w16, ld_w, col0, cols, src, need_grad):
+    """Steps 2-5 through the peer buffers: returns token_loss, token_entropy, correct (int32)
+    and the reduced fp16 gradient [N, cols] (or None)."""
     lib = _lib.load()
     device = stats.device
     stream = _lib.stream_of(device)
@@ -227,72 +196,25 @@ def _peer_block(ex, stats, acc, rows_targets, n_grad, w16, ld_w, col0, cols, nee
     _lib.check(lib.talm_head_merge_peers(n_tokens, cols, ex.rank, ex.world, n_grad, own, epoch,
                                          _lib.ptr(merged), _lib.ptr(scale), stream),
                "talm_head_merge_peers")
+    token_loss = torch.empty(n_tokens, dtype=torch.float32, device=device)
+    token_entropy = torch.empty_like(token_loss)
+    correct = torch.empty(n_tokens, dtype=torch.int32, device=device)
     if not need_grad:
         _lib.check(lib.talm_head_finalize(
             _lib.ptr(merged), _lib.ptr(rows_targets), n_tokens, 0, None, None, _lib.ptr(w16),
-            ld_w, col0, w16.shape[0], cols, None, _lib.ptr(token_loss),
+            ld_w, col0, w16.shape[0], cols, _lib.ptr(src), _lib.ptr(token_loss),
             _lib.ptr(token_entropy), _lib.ptr(correct), None, 0, stream), "talm_head_finalize")
-        return
+        return token_loss, token_entropy, correct, None
     _lib.check(lib.talm_head_finalize_scatter(
         _lib.ptr(merged), _lib.ptr(rows_targets), n_tokens, n_grad, _lib.ptr(acc),
-        _lib.ptr(scale), _lib.ptr(w16), ld_w, col0, w16.shape[0], cols, None,
+        _lib.ptr(scale), _lib.ptr(w16), ld_w, col0, w16.shape[0], cols, _lib.ptr(src),
         _lib.ptr(token_loss), _lib.ptr(token_entropy), _lib.ptr(correct), ex.rank, ex.world,
         peers, epoch, stream), "talm_head_finalize_scatter")
     _lib.check(lib.talm_head_reduce_gather(n_tokens, cols, ex.rank, ex.world, peers, epoch,
                                            stream), "talm_head_reduce_gather")
+    grad = torch.empty(n_tokens, cols, dtype=torch.float16, device=device)
     _lib.check(lib.talm_head_gather_finish(n_tokens, cols, ex.world, own, epoch,
                                            _lib.ptr(grad), stream), "talm_head_gather_finish")
-
-
-def _peer_flow(group, ops, h16, w16, ld_w, rows_targets, n_grad, cols, col0, vocab_chunk,
-               need_grad):
-    """Steps 1-5 of the peer flow in token blocks. Block b walks the vocabulary on the current
-    stream; the exchange of every block but the last runs on a side stream while the next block
-    walks with `EXCHANGE_SMS` SMs left free for it; the last block's exchange follows its walk.
-    Returns token_loss, token_entropy, correct (int32) and the reduced fp16 gradient [N, cols]
-    (or None), in the rows' order (labelled-first when compacted). None when the ranks cannot
-    map each other's memory (the caller then uses the NCCL flow)."""
-    lib = _lib.load()
-    device = h16.device
-    n_tokens = h16.shape[0]
-    blocks = token_blocks(n_tokens)
-    exchanges = [_exchange(group, device, r1 - r0, cols, b) for b, (r0, r1) in enumerate(blocks)]
-    if any(ex is None for ex in exchanges):
-        return None
-    token_loss = torch.empty(n_tokens, dtype=torch.float32, device=device)
-    token_entropy = torch.empty_like(token_loss)
-    correct = torch.empty(n_tokens, dtype=torch.int32, device=device)
-    grad = torch.empty(n_tokens, cols, dtype=torch.float16, device=device) if need_grad else None
-    main = torch.cuda.current_stream(device)
-    side = _side_stream(device) if len(blocks) > 1 else None
-    sms = torch.cuda.get_device_properties(device).multi_processor_count
-    for b, (r0, r1) in enumerate(blocks):
-        ng = min(max(n_grad - r0, 0), r1 - r0)
-        targets_b = rows_targets[r0:r1]
-        if b > 0:  # an earlier block's exchange runs beside this walk
-            _lib.check(lib.talm_head_set_sm_budget(max(sms - EXCHANGE_SMS, 2)),
-                       "talm_head_set_sm_budget")
-        try:
-            stats, acc = ops.shard(h16[r0:r1], w16, ld_w, targets_b, ng, cols, col0,
-                                   vocab_chunk)
-        finally:
-            if b > 0:
-                lib.talm_head_set_sm_budget(0)
-        outs = (token_loss[r0:r1], token_entropy[r0:r1], correct[r0:r1],
-                grad[r0:r1] if need_grad else None)
-        if b == len(blocks) - 1:
-            _peer_block(exchanges[b], stats, acc, targets_b, ng, w16, ld_w, col0, cols,
-                        need_grad, *outs)
-            continue
-        side.wait_stream(main)
-        with torch.cuda.stream(side):
-            _peer_block(exchanges[b], stats, acc, targets_b, ng, w16, ld_w, col0, cols,
-                        need_grad, *outs)
-        for t in (stats, acc, rows_targets):
-            if t is not None:
-                t.record_stream(side)
-    if side is not None:
-        main.wait_stream(side)
     return token_loss, token_entropy, correct, grad
 
 
@@ -321,24 +243,18 @@ def sharded_head(hidden, weight_shard, targets, vocab, col0, num_items=None, voc
             h16 = h16.index_select(0, src)
             rows_targets = targets.index_select(0, src)
 
-    peer = None
-    if PEER_EXCHANGE and isinstance(ops, CudaHeadOps) and world > 1 and n_tokens > 0:
-        peer = _peer_flow(group, ops, h16, w16, ld_w, rows_targets, n_grad, cols, col0,
-                          int(vocab_chunk), need_grad)
-    if peer is not None:
-        token_loss, token_entropy, correct, grad = peer
-        if src is not None:  # back to the caller's row order
-            token_loss = torch.empty_like(token_loss).index_copy_(0, src, token_loss)
-            token_entropy = torch.empty_like(token_entropy).index_copy_(0, src, token_entropy)
-            correct = torch.empty_like(correct).index_copy_(0, src, correct)
-            if grad is not None:
-                grad = torch.empty_like(grad).index_copy_(0, src, grad)
+    stats, acc = ops.shard(h16, w16, ld_w, rows_targets, n_grad, cols, col0, int(vocab_chunk))
+    ex = (_exchange(group, stats.device, n_tokens, cols)
+          if PEER_EXCHANGE and isinstance(ops, CudaHeadOps) and world > 1 and n_tokens > 0
+          else None)
+    if ex is not None:
+        token_loss, token_entropy, correct, grad = _peer_flow(
+            ex, stats, acc, rows_targets, n_grad, w16, ld_w, col0, cols, src, need_grad)
         if grad is not None:
             grad = grad[:, :hidden_size]
         denom = _denominator(num_items, labelled.sum())
         loss = token_loss.sum() / denom
         return loss, token_loss, token_entropy, correct.to(torch.bool), grad
-    stats, acc = ops.shard(h16, w16, ld_w, rows_targets, n_grad, cols, col0, int(vocab_chunk))
     gathered = torch.empty(world * n_tokens, _lib.HEAD_STATS, dtype=torch.float32,
                            device=stats.device)
     dist.all_gather_into_tensor(gathered, stats, group=group)

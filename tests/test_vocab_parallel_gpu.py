@@ -46,9 +46,6 @@ def _worker(rank, world, port, q, sizes, vocab, size, flow):
         from talm_b200.vocab_parallel import shard_bounds, vocab_parallel_head_loss
 
         vocab_parallel.PEER_EXCHANGE = flow != "nccl"
-        if flow == "peer_blocks":  # the two-block walk with the first exchange overlapped
-            vocab_parallel.SPLIT_MIN_ROWS = 128
-            assert len(vocab_parallel.token_blocks(sizes[0])) == 2
         col0, cols = shard_bounds(vocab, world, rank)
         results = []
         # several calls: the peer buffers are reused (epochs) and grow once (600 -> 1500 rows)
@@ -70,10 +67,9 @@ def _worker(rank, world, port, q, sizes, vocab, size, flow):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("flow", ["peer", "peer_blocks", "nccl"])
+@pytest.mark.parametrize("flow", ["peer", "nccl"])
 def test_vocab_parallel_matches_single_gpu(flow):
-    """Both exchange flows: the library's NVLink peer exchange (one token block, and two blocks
-    with the first block's exchange beside the second block's walk) and NCCL collectives."""
+    """Both exchange flows: the library's NVLink peer exchange and NCCL collectives."""
     world = torch.cuda.device_count()
     if world < 2:
         pytest.skip("needs 2 or more GPUs")
