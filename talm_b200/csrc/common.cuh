@@ -117,18 +117,32 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 // Bounded wait for the phase with the given parity to complete. `abort` (shared) is set by the
 // first wait of the CTA that gives up, so that every other role stops waiting at once.
 // Returns false when the wait gave up or the CTA is aborting.
+// The polls of a bounded wait between two looks at the clock: the loop that reacts to the
+// barrier holds no clock read and no global load, so a phase that completes while the thread
+// spins is seen at once; the clock (and the limit, a global load) is read every 64 polls, which
+// is a few microseconds at most.
+constexpr uint32_t kPollsPerClockCheck = 64;
+
+// Bounded wait for the phase with the given parity to complete. `abort` (shared) is set by the
+// first wait of the CTA that gives up, so that every other role stops waiting at once.
+// Returns false when the wait gave up or the CTA is aborting.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile int* abort) {
   if (mbar_test(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  const uint64_t limit = wait_limit_ns();
-  while (true) {
+  uint64_t t0 = 0, limit = 0;
+  for (uint32_t poll = 1;; ++poll) {
     if (mbar_test(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer_ns() - t0 > limit) {
-      *abort = 1;
-      record_timeout();
-      return false;
+    if (poll % kPollsPerClockCheck == 0) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+        limit = wait_limit_ns();
+      } else if (now - t0 > limit) {
+        *abort = 1;
+        record_timeout();
+        return false;
+      }
     }
   }
 }
@@ -136,12 +150,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
 // Bounded wait that ignores the CTA's abort flag: used on the way out, to let copies and MMAs
 // already in flight land before shared memory and TMEM are released.
 __device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
-  const uint64_t t0 = globaltimer_ns();
-  const uint64_t limit = wait_limit_ns();
-  while (!mbar_test(bar, parity)) {
-    if (globaltimer_ns() - t0 > limit) {
-      record_timeout();
-      return false;
+  uint64_t t0 = 0, limit = 0;
+  for (uint32_t poll = 1; !mbar_test(bar, parity); ++poll) {
+    if (poll % kPollsPerClockCheck == 0) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+        limit = wait_limit_ns();
+      } else if (now - t0 > limit) {
+        record_timeout();
+        return false;
+      }
     }
   }
   return true;

@@ -117,15 +117,20 @@ __device__ __forceinline__ bool mbar_test_cluster(uint64_t* bar, uint32_t parity
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort) {
   if (mbar_test_cluster(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  const uint64_t limit = wait_limit_ns();
-  while (true) {
+  uint64_t t0 = 0, limit = 0;
+  for (uint32_t poll = 1;; ++poll) {
     if (mbar_test_cluster(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer_ns() - t0 > limit) {
-      *abort = 1;
-      record_timeout();
-      return false;
+    if (poll % kPollsPerClockCheck == 0) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+        limit = wait_limit_ns();
+      } else if (now - t0 > limit) {
+        *abort = 1;
+        record_timeout();
+        return false;
+      }
     }
   }
 }
