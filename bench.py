@@ -155,10 +155,14 @@ def timed(fn, steps, world, label=None, kernels=False):
     start.record()
     if kernels:
         _lib.profile_begin()
+    # an NVTX range around the timed loop, so that a profiler can keep exactly these launches
+    # (ncu --nvtx --nvtx-include "timed_<label>/")
+    torch.cuda.nvtx.range_push(f"timed_{label or 'loop'}")
     t0 = time.perf_counter()
     for _ in range(steps):
         fn()
     host = (time.perf_counter() - t0) * 1000
+    torch.cuda.nvtx.range_pop()
     stop.record()
     barrier(world)
     if kernels:
