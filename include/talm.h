@@ -259,8 +259,11 @@ int talm_head_scale_grad(const void* grad, int64_t ld_grad, int grad_is_f32,
  * other ranks' buffers with talm_ipc_import. `peers` is a device array of `world` uint64 device
  * addresses: peers[q] = rank q's buffer as mapped in this process (peers[rank] = its own).
  * `epoch` numbers the call (1, 2, ...; the same on every rank). One call is, in stream order:
- *   talm_head_publish_stats  -> talm_head_merge_peers -> talm_head_finalize_scatter
- *   -> talm_head_reduce_gather -> talm_head_gather_finish
+ *   talm_head_shard -> talm_head_publish_stats -> talm_head_merge_peers
+ *   -> talm_head_finalize_scatter -> talm_head_reduce_gather -> talm_head_gather_finish
+ * or, with the scatter inside the walk's last accumulator GEMM:
+ *   talm_head_shard_begin -> talm_head_publish_stats -> talm_head_merge_peers
+ *   -> talm_head_shard_finish_scatter -> talm_head_reduce_gather -> talm_head_gather_finish
  * Kernels of different ranks wait on each other through flags in the peer buffers; every wait
  * is bounded (2 s, then TALM_ETIMEOUT in talm_device_status and the kernel returns). */
 #define TALM_IPC_HANDLE_BYTES 64
@@ -287,6 +290,30 @@ int talm_head_finalize_scatter(const float* stats, const int64_t* targets, int64
                                float* token_entropy, int32_t* correct, int64_t rank,
                                int64_t world, const uint64_t* peers, uint32_t epoch,
                                void* stream);
+/* talm_head_shard without its last step (the accumulator GEMM of the last slice, which no
+ * logits GEMM precedes): the statistics are final when it returns, acc still lacks the last
+ * slice. Same arguments and preconditions as talm_head_shard. */
+int talm_head_shard_begin(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* weight,
+                          int64_t ld_weight, const int64_t* targets, int64_t n_tokens,
+                          int64_t n_grad, int64_t hidden_size, int64_t vocab_cols,
+                          int64_t vocab_col0, int64_t vocab_chunk, float* stats, float* acc,
+                          void* workspace, size_t ws_bytes, void* stream);
+/* Phase 1 for a walk run by talm_head_shard_begin, in place of talm_head_finalize_scatter:
+ * the per-row outputs from the merged `stats` (and zero gradient rows for rows n_grad..), then
+ * the walk's last step, whose epilogue finishes each gradient row -- (acc + last slice) *
+ * acc_scale minus the owned target weight row, the values talm_head_finalize_scatter computes
+ * -- and stores it in fp32 at its owner, overlapping the scatter with the step's MMAs. The walk
+ * arguments (weight .. vocab_chunk, acc, workspace) are those of the talm_head_shard_begin
+ * call; acc 16-byte and the weight rows 8-byte aligned. */
+int talm_head_shard_finish_scatter(const uint16_t* weight, int64_t ld_weight,
+                                   const int64_t* targets, int64_t n_tokens, int64_t n_grad,
+                                   int64_t hidden_size, int64_t vocab_cols, int64_t vocab_col0,
+                                   int64_t vocab_chunk, const float* stats, float* acc,
+                                   const float* acc_scale, void* workspace, size_t ws_bytes,
+                                   const int64_t* grad_rows, float* token_loss,
+                                   float* token_entropy, int32_t* correct, int64_t rank,
+                                   int64_t world, const uint64_t* peers, uint32_t epoch,
+                                   void* stream);
 /* Phase 2: waits for every rank's rows, sums the rows this rank owns over the ranks in rank
  * order (fp32), rounds them to fp16 and writes them into every rank's buffer. */
 int talm_head_reduce_gather(int64_t n_tokens, int64_t hidden, int64_t rank, int64_t world,

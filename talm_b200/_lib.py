@@ -50,6 +50,11 @@ SIGNATURES = {
     "talm_head_merge_peers": (_INT, [_I64, _I64, _I64, _I64, _I64, _P, _U32, _P, _P, _P]),
     "talm_head_finalize_scatter": (_INT, [_P, _P, _I64, _I64, _P, _P, _P, _I64, _I64, _I64,
                                           _I64, _P, _P, _P, _P, _I64, _I64, _P, _U32, _P]),
+    "talm_head_shard_begin": (_INT, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64,
+                                     _I64, _P, _P, _P, _SZ, _P]),
+    "talm_head_shard_finish_scatter": (_INT, [_P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64,
+                                              _P, _P, _P, _P, _SZ, _P, _P, _P, _P, _I64, _I64,
+                                              _P, _U32, _P]),
     "talm_head_reduce_gather": (_INT, [_I64, _I64, _I64, _I64, _P, _U32, _P]),
     "talm_head_gather_finish": (_INT, [_I64, _I64, _I64, _P, _U32, _P, _P]),
 }

@@ -329,9 +329,42 @@ struct AccumParams {
 // share one persistent grid of CTA pairs, so that the accumulator work fills the logits GEMM's
 // last, partial wave (and vice versa) and a slice costs two launches (this and the combine).
 // ------------------------------------------------------------------------------------------
+// One element of a gradient row under a merged scale (the vocabulary-parallel flows):
+// a * scale, minus the target's weight where this rank holds the target column, 0 for a row
+// without gradient; each operation rounded on its own (no contraction into an FMA), so that
+// the scatter epilogue and head_finalize_kernel give the same bits.
+__device__ __forceinline__ float grad_value(bool live, bool own, float a, float scale, float w) {
+  if (!live) return 0.0f;
+  const float g = __fmul_rn(a, scale);
+  return own ? __fsub_rn(g, w) : g;
+}
+
+// The last accumulator step of a vocabulary-parallel walk under the peer exchange
+// (talm_head_shard_finish_scatter): instead of adding its tiles into acc, the epilogue
+// finishes each piece of a gradient row -- (acc + D) * scale[row], minus the target's weight
+// row where this rank holds the target column, 0 for an unlabelled row; the arithmetic of
+// head_finalize_kernel after a reduce-add of D -- and stores it in fp32 straight into the
+// owning rank's receive slot over NVLink, so that the scatter overlaps the step's MMAs. The
+// last CTA to finish raises this rank's phase-1 flag on every rank.
+struct ScatterParams {
+  int on;
+  int tile_shift;                   // accumulator tiles are taken from this one on (rotated)
+  const float* acc;                 // [n_grad][hidden]: the earlier slices' sum
+  const float* scale;               // [n_grad]: e^(REF - REF_merged) / S_merged
+  const long long* targets;         // [n_tokens], in row order
+  const long long* grad_rows;       // output row of each row (null: the row itself)
+  const __half* weight;             // this rank's weight rows
+  long long ld_weight, col0, vcols;
+  const unsigned long long* peers;  // every rank's peer buffer, mapped here
+  peer::PeerLayout L;
+  int rank, world;
+  uint32_t epoch;
+};
+
 struct SliceParams {
   LogitsParams lg;  // logits GEMM of slice s: n_tiles_l pair tiles (0: none, the last step)
   AccumParams ac;   // accumulator GEMM of slice s - 1: n_tiles_a pair tiles (0: none)
+  ScatterParams sc; // sc.on: the accumulator tiles finish the rows and scatter them
   int n_tiles_l;
   int n_tiles_a;
 };
@@ -381,6 +414,7 @@ __device__ __forceinline__ bool slice_unit(const SliceParams& p, const PairPlan&
   if (u < plan.n_a) {
     out.type = 1;
     out.tile = pair + u * n_pairs;
+    if (p.sc.on) out.tile = (out.tile + p.sc.tile_shift) % p.n_tiles_a;
     out.kb1 = p.ac.k_blocks;
     return true;
   }
@@ -675,6 +709,60 @@ __global__ void __launch_bounds__(SLICE_THREADS, 1)
             st[TALM_STAT_HIT] = 1.0f;
           }
         }
+      } else if (p.sc.on) {  // the walk's last accumulator step: finish the rows, send them
+        const ScatterParams& sc = p.sc;
+        const int ht = unit.tile % ap.n_h_tiles, pr = unit.tile / ap.n_h_tiles;
+        const int row = pr * PAIR_ROWS + static_cast<int>(rank) * BM + r_in_tile;
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+        const bool valid = row < ap.n_grad;
+        const long long tgt = valid ? sc.targets[row] : -1;
+        const bool live = tgt >= 0;
+        const bool own = live && tgt >= sc.col0 && tgt < sc.col0 + sc.vcols;
+        const float scale = live ? sc.scale[row] : 0.0f;
+        const long long out = valid ? (sc.grad_rows ? sc.grad_rows[row] : row) : 0;
+        const long long owner = out / sc.L.rpr;
+        float* const dst =
+            reinterpret_cast<float*>(sc.peers[valid ? owner : sc.rank] + sc.L.recv) +
+            (static_cast<long long>(sc.rank) * sc.L.rpr + (out - owner * sc.L.rpr)) * ap.hidden;
+        const float* const arow = sc.acc + static_cast<long long>(valid ? row : 0) * ap.hidden;
+        const __half* const wrow = sc.weight + (own ? (tgt - sc.col0) * sc.ld_weight : 0);
+  #pragma unroll 1
+        for (int c = g * (EPI_COLS / 32); c < (g + 1) * (EPI_COLS / 32); ++c) {
+          const int h0 = ht * BN + c * 32;
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, r);
+          // the earlier slices' sums load while the TMEM load is in flight
+          float4 a[8];
+  #pragma unroll
+          for (int v = 0; v < 8; ++v)
+            a[v] = (valid && h0 + 4 * v < ap.hidden)
+                       ? *reinterpret_cast<const float4*>(arow + h0 + 4 * v)
+                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          tmem_wait_ld();
+          if (!valid) continue;
+  #pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            const int h = h0 + 4 * v;
+            if (h >= ap.hidden) break;
+            float w[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (own) {
+              const uint2 wv = *reinterpret_cast<const uint2*>(wrow + h);
+              const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
+              const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
+              w[0] = w01.x; w[1] = w01.y; w[2] = w23.x; w[3] = w23.y;
+            }
+            // acc + D as the reduce-add of the other steps forms it, then the finalize
+            const float4 o = make_float4(
+                grad_value(live, own, __fadd_rn(a[v].x, __uint_as_float(r[4 * v])), scale, w[0]),
+                grad_value(live, own, __fadd_rn(a[v].y, __uint_as_float(r[4 * v + 1])), scale, w[1]),
+                grad_value(live, own, __fadd_rn(a[v].z, __uint_as_float(r[4 * v + 2])), scale, w[2]),
+                grad_value(live, own, __fadd_rn(a[v].w, __uint_as_float(r[4 * v + 3])), scale, w[3]));
+            *reinterpret_cast<float4*>(dst + h) = o;
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&ctl->tempty[acc]), 0));
       } else {  // accumulator K range: acc += D
         const int ht = unit.tile % ap.n_h_tiles, pr = unit.tile / ap.n_h_tiles;
         const int row0 = pr * PAIR_ROWS + static_cast<int>(rank) * BM;
@@ -714,6 +802,9 @@ __global__ void __launch_bounds__(SLICE_THREADS, 1)
     if (elected) bulk_wait_all();  // every store and reduce has landed before the CTA leaves
   }
   pair_teardown(ctl, warp, tmem_base);
+  if (p.sc.on)  // every gradient row piece of this CTA has been stored at its owner
+    peer::cta_signal_phase(reinterpret_cast<uint8_t*>(p.sc.peers[p.sc.rank]), p.sc.peers,
+                           p.sc.L.flags, p.sc.L.counters, 1, p.sc.rank, p.sc.world, p.sc.epoch);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -728,6 +819,8 @@ struct GradDest {
   size_t recv_off;
   long long rpr;                    // rows per rank
   int rank;
+  long long grad_from;              // rows below this one get no gradient row here
+  int signal;                       // peers: the kernel ends phase 1 (raises the flags)
   __device__ __forceinline__ void* row_ptr(long long out, int hidden) const {
     if (peers == nullptr) {
       return grad_f32 ? static_cast<void*>(static_cast<float*>(grad) + out * hidden)
@@ -760,7 +853,7 @@ __device__ __forceinline__ void finalize_row(
       correct[out] = (labelled && static_cast<long long>(__float_as_int(st[TALM_STAT_IDX])) == tgt)
                          ? 1 : 0;
   }
-  if (dest.grad == nullptr && dest.peers == nullptr) return;
+  if ((dest.grad == nullptr && dest.peers == nullptr) || row < dest.grad_from) return;
   const int grad_f32 = dest.peers != nullptr ? 1 : dest.grad_f32;
   void* const grow = dest.row_ptr(out, hidden);
   const bool live = labelled && row < n_grad && acc != nullptr;
@@ -769,8 +862,9 @@ __device__ __forceinline__ void finalize_row(
   const __half* wrow = weight + (own ? (tgt - col0) * ld_weight : 0);
   const float scale = acc_scale ? acc_scale[row] : 0.0f;
   auto value = [&](float a, __half w) {
+    if (acc_scale) return grad_value(live, own, a, scale, __half2float(w));
     if (!live) return 0.0f;
-    const float g = acc_scale ? a * scale : a / s;
+    const float g = a / s;
     return own ? g - __half2float(w) : g;
   };
   if (vec4) {  // 4 columns per lane and step: 16-byte acc loads, 8- or 16-byte stores
@@ -827,9 +921,12 @@ __global__ void __launch_bounds__(256) head_finalize_kernel(
   if (row < n_tokens)
     finalize_row(row, lane, stats, targets, n_grad, acc, acc_scale, weight, ld_weight, col0,
                  vcols, hidden, grad_rows, token_loss, token_entropy, correct, dest, vec4);
-  if (dest.peers != nullptr)
+  if (dest.peers != nullptr && dest.signal) {
     peer::cta_signal_phase(reinterpret_cast<uint8_t*>(dest.peers[dest.rank]), dest.peers,
                            L.flags, L.counters, 1, dest.rank, world, epoch);
+  } else if (dest.peers != nullptr) {
+    __threadfence_system();  // the zero rows; the scatter step after this kernel signals
+  }
 }
 
 // ------------------------------------------------------------------------------------------
@@ -1125,30 +1222,20 @@ int launch_slice_step(const CUtensorMap& tm_hidden, const CUtensorMap& tm_weight
 // Pairs that fit on the GPU at once (one CTA per SM: shared memory and TMEM are taken whole).
 int max_pairs_of(int sms) { return sms / 2 > 0 ? sms / 2 : 1; }
 
+// Which steps of a walk one call runs: all of them; all but the last (accumulator-only) step,
+// whose accumulator GEMM talm_head_shard_finish_scatter then runs with the scatter epilogue
+// once the statistics are merged; or only that last step.
+enum WalkPart { WALK_ALL, WALK_BEGIN, WALK_LAST };
 
-}  // namespace head
-}  // namespace talm
-
-extern "C" {
-
-int talm_head_workspace_size(int64_t n_tokens, int64_t n_grad, int64_t hidden,
-                             int64_t vocab_cols, int64_t vocab_chunk, size_t* bytes) {
-  using namespace talm;
-  if (bytes == nullptr) return set_error(TALM_EINVAL, "bytes is NULL");
-  if (n_tokens < 0 || n_grad < 0 || n_grad > n_tokens || hidden < 1 || vocab_cols < 1)
-    return set_error(TALM_EINVAL, "bad sizes");
-  *bytes = head::layout(n_tokens, n_grad, vocab_cols, vocab_chunk, nullptr).bytes;
-  return TALM_OK;
-}
-
-int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* weight,
-                    int64_t ld_weight, const int64_t* targets, int64_t n_tokens, int64_t n_grad,
-                    int64_t hidden_size, int64_t vocab_cols, int64_t vocab_col0,
-                    int64_t vocab_chunk, float* stats, float* acc, void* workspace,
-                    size_t ws_bytes, void* stream_) {
-  using namespace talm;
-  using namespace talm::head;
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+// The vocabulary walk over weight rows [0, vocab_cols) of `weight` (global columns vocab_col0..):
+// step k < n_slices runs the logits GEMM of slice k together with the accumulator GEMM of slice
+// k - 1, then the combine of slice k; step n_slices runs the accumulator GEMM of the last
+// slice. `sc` (WALK_LAST only) turns that last accumulator GEMM into the scatter step.
+int shard_walk(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* weight,
+               int64_t ld_weight, const int64_t* targets, int64_t n_tokens, int64_t n_grad,
+               int64_t hidden_size, int64_t vocab_cols, int64_t vocab_col0, int64_t vocab_chunk,
+               float* stats, float* acc, void* workspace, size_t ws_bytes, cudaStream_t stream,
+               WalkPart part, const ScatterParams* sc) {
   if (n_tokens < 0 || n_grad < 0 || n_grad > n_tokens)
     return set_error(TALM_EINVAL, "need 0 <= n_grad <= n_tokens");
   if (hidden_size < 8 || hidden_size % 8 != 0 || ld_hidden % 8 != 0 || ld_weight % 8 != 0 ||
@@ -1158,8 +1245,10 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
   if (n_tokens >= (int64_t{1} << 30) || vocab_cols >= (int64_t{1} << 31) ||
       hidden_size >= (int64_t{1} << 20))
     return set_error(TALM_ERANGE, "sizes beyond the kernels' 32-bit tile indices");
-  if (n_tokens == 0) return TALM_OK;
-  if (!hidden || !weight || !targets || !stats || (n_grad > 0 && !acc) || !workspace)
+  if (n_tokens == 0 || (part == WALK_LAST && n_grad == 0)) return TALM_OK;
+  const bool logits_steps = part != WALK_LAST;
+  if ((logits_steps && !hidden) || !weight || !targets || !stats || (n_grad > 0 && !acc) ||
+      !workspace)
     return set_error(TALM_EINVAL, "null pointer");
   if (!device_is_sm100()) return set_error(TALM_ENODEV, "the head kernels need an sm_100 GPU");
   uint8_t* base = reinterpret_cast<uint8_t*>(
@@ -1173,37 +1262,48 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
   const int sms = current_sm_count();
 
   CUtensorMap tm_hidden, tm_weight, tm_weight_mn;
-  st = talm_make_tmap_2d_f16(&tm_hidden, hidden, hidden_size, n_tokens, ld_hidden, BK, BM);
-  if (st == TALM_OK)
-    st = talm_make_tmap_2d_f16(&tm_weight, weight, hidden_size, vocab_cols, ld_weight, BK, BN / 2);
+  st = TALM_OK;
+  if (logits_steps) {
+    st = talm_make_tmap_2d_f16(&tm_hidden, hidden, hidden_size, n_tokens, ld_hidden, BK, BM);
+    if (st == TALM_OK)
+      st = talm_make_tmap_2d_f16(&tm_weight, weight, hidden_size, vocab_cols, ld_weight, BK,
+                                 BN / 2);
+  }
   if (st == TALM_OK && n_grad > 0)
     st = talm_make_tmap_2d_f16(&tm_weight_mn, weight, hidden_size, vocab_cols, ld_weight, 64, BK);
-  CUtensorMap tm_acc = tm_hidden;
-  if (st == TALM_OK && n_grad > 0)
-    st = talm_make_tmap_2d_f32(&tm_acc, acc, hidden_size, n_grad, hidden_size, 32, BM);
   if (st != TALM_OK) return st;
+  if (!logits_steps) tm_hidden = tm_weight = tm_weight_mn;  // unused by an accumulator step
+  CUtensorMap tm_acc = tm_hidden;
+  if (n_grad > 0 && (st = talm_make_tmap_2d_f32(&tm_acc, acc, hidden_size, n_grad, hidden_size,
+                                                32, BM)) != TALM_OK)
+    return st;
 
   const Slices sl = slices_of(vocab_cols, chunk);
   const int64_t n_slices = sl.count;
+  const int64_t k_first = part == WALK_LAST ? n_slices : 0;
+  const int64_t k_last = part == WALK_BEGIN ? n_slices - 1 : n_slices;
 
-  if (cudaMemsetAsync(stats, 0, sizeof(float) * TALM_HEAD_STATS * n_tokens, stream) != cudaSuccess)
-    return check_launch("stats memset");
-  // every accumulator GEMM adds into acc (TMA reduce-add): it starts at zero
-  if (n_grad > 0 &&
-      cudaMemsetAsync(acc, 0, sizeof(float) * n_grad * hidden_size, stream) != cudaSuccess)
-    return check_launch("acc memset");
+  if (k_first == 0) {
+    if (cudaMemsetAsync(stats, 0, sizeof(float) * TALM_HEAD_STATS * n_tokens, stream) !=
+        cudaSuccess)
+      return check_launch("stats memset");
+    // every accumulator GEMM adds into acc (TMA reduce-add): it starts at zero
+    if (n_grad > 0 &&
+        cudaMemsetAsync(acc, 0, sizeof(float) * n_grad * hidden_size, stream) != cudaSuccess)
+      return check_launch("acc memset");
+  }
 
   const int k_blocks = static_cast<int>((hidden_size + BK - 1) / BK);
   const int n_pair_rows = static_cast<int>((n_tokens + PAIR_ROWS - 1) / PAIR_ROWS);
   const int max_pairs = max_pairs_of(sms);
-  // Step k runs the logits GEMM of slice k (k < n_slices) together with the accumulator GEMM
-  // of slice k - 1 (k >= 1), then the combine of slice k. The slices' probability buffers
-  // alternate: step k writes buffer k % 2 while its accumulator part reads buffer (k - 1) % 2.
-  // The combine of slice k follows the accumulator GEMM of slice k - 1 (its acc rescale needs
-  // that) and precedes the one of slice k (which reads the rows it rescales).
+  // The slices' probability buffers alternate: step k writes buffer k % 2 while its
+  // accumulator part reads buffer (k - 1) % 2. The combine of slice k follows the accumulator
+  // GEMM of slice k - 1 (its acc rescale needs that) and precedes the one of slice k (which
+  // reads the rows it rescales). Steps before k_first are only planned, not launched.
   AccumParams prev_ap{};
   CUtensorMap prev_tm_probs = tm_hidden;
-  for (int64_t k = 0; k <= n_slices; ++k) {
+  for (int64_t k = 0; k <= k_last; ++k) {
+    const bool run = k >= k_first;
     SliceParams sp{};
     sp.n_tiles_l = 0;
     sp.n_tiles_a = 0;
@@ -1239,14 +1339,15 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
       sp.ac = prev_ap;
       sp.n_tiles_a = prev_ap.n_pair_rows * prev_ap.n_h_tiles;
     }
-    if (sp.n_tiles_l + sp.n_tiles_a > 0) {
+    if (k == n_slices && sc != nullptr) sp.sc = *sc;
+    if (run && sp.n_tiles_l + sp.n_tiles_a > 0) {
       LaunchTimer timer(TALM_KERNEL_HEAD_SLICE, stream);
       st = launch_slice_step(tm_hidden, tm_weight, tm_probs_out, prev_tm_probs, tm_weight_mn,
                              tm_acc, sp, stream, max_pairs);
       if (st != TALM_OK) return st;
     }
     if (k == n_slices) break;
-    {
+    if (run) {
       LaunchTimer timer(TALM_KERNEL_HEAD_COMBINE, stream);
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(static_cast<unsigned>((n_tokens + 7) / 8), 1, 1);
@@ -1276,6 +1377,111 @@ int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* w
     prev_tm_probs = tm_probs_out;
   }
   return TALM_OK;
+}
+
+
+}  // namespace head
+}  // namespace talm
+
+extern "C" {
+
+int talm_head_workspace_size(int64_t n_tokens, int64_t n_grad, int64_t hidden,
+                             int64_t vocab_cols, int64_t vocab_chunk, size_t* bytes) {
+  using namespace talm;
+  if (bytes == nullptr) return set_error(TALM_EINVAL, "bytes is NULL");
+  if (n_tokens < 0 || n_grad < 0 || n_grad > n_tokens || hidden < 1 || vocab_cols < 1)
+    return set_error(TALM_EINVAL, "bad sizes");
+  *bytes = head::layout(n_tokens, n_grad, vocab_cols, vocab_chunk, nullptr).bytes;
+  return TALM_OK;
+}
+
+int talm_head_shard(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* weight,
+                    int64_t ld_weight, const int64_t* targets, int64_t n_tokens, int64_t n_grad,
+                    int64_t hidden_size, int64_t vocab_cols, int64_t vocab_col0,
+                    int64_t vocab_chunk, float* stats, float* acc, void* workspace,
+                    size_t ws_bytes, void* stream) {
+  return talm::head::shard_walk(hidden, ld_hidden, weight, ld_weight, targets, n_tokens, n_grad,
+                                hidden_size, vocab_cols, vocab_col0, vocab_chunk, stats, acc,
+                                workspace, ws_bytes, static_cast<cudaStream_t>(stream),
+                                talm::head::WALK_ALL, nullptr);
+}
+
+int talm_head_shard_begin(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* weight,
+                          int64_t ld_weight, const int64_t* targets, int64_t n_tokens,
+                          int64_t n_grad, int64_t hidden_size, int64_t vocab_cols,
+                          int64_t vocab_col0, int64_t vocab_chunk, float* stats, float* acc,
+                          void* workspace, size_t ws_bytes, void* stream) {
+  return talm::head::shard_walk(hidden, ld_hidden, weight, ld_weight, targets, n_tokens, n_grad,
+                                hidden_size, vocab_cols, vocab_col0, vocab_chunk, stats, acc,
+                                workspace, ws_bytes, static_cast<cudaStream_t>(stream),
+                                talm::head::WALK_BEGIN, nullptr);
+}
+
+int talm_head_shard_finish_scatter(const uint16_t* weight, int64_t ld_weight,
+                                   const int64_t* targets, int64_t n_tokens, int64_t n_grad,
+                                   int64_t hidden_size, int64_t vocab_cols, int64_t vocab_col0,
+                                   int64_t vocab_chunk, const float* stats, float* acc,
+                                   const float* acc_scale, void* workspace, size_t ws_bytes,
+                                   const int64_t* grad_rows, float* token_loss,
+                                   float* token_entropy, int32_t* correct, int64_t rank,
+                                   int64_t world, const uint64_t* peers, uint32_t epoch,
+                                   void* stream) {
+  using namespace talm;
+  if (n_tokens < 0 || n_grad < 0 || n_grad > n_tokens)
+    return set_error(TALM_EINVAL, "need 0 <= n_grad <= n_tokens");
+  int st = peer::check_peer_args(world, rank, n_tokens, hidden_size);
+  if (st != TALM_OK) return st;
+  if (n_grad == 0)  // no accumulator: the finalize kernel ends phase 1 itself
+    return talm_head_finalize_scatter(stats, targets, n_tokens, 0, nullptr, nullptr, weight,
+                                      ld_weight, vocab_col0, vocab_cols, hidden_size,
+                                      grad_rows, token_loss, token_entropy, correct, rank,
+                                      world, peers, epoch, stream);
+  if (!peers || !stats || !targets || !acc || !acc_scale || !weight)
+    return set_error(TALM_EINVAL, "null pointer");
+  if (ld_weight % 4 != 0 || (reinterpret_cast<uintptr_t>(weight) & 7) != 0 ||
+      (reinterpret_cast<uintptr_t>(acc) & 15) != 0)
+    return set_error(TALM_EINVAL, "acc must be 16-byte and the weight rows 8-byte aligned");
+  const peer::PeerLayout L = peer::peer_layout(world, n_tokens, hidden_size);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  {
+    // the per-row outputs, and zero gradient rows for the rows without one (n_grad and on);
+    // the rows below n_grad leave from the scatter step
+    LaunchTimer timer(TALM_KERNEL_HEAD_FINALIZE, s);
+    head::head_finalize_kernel<<<static_cast<int>((n_tokens + 7) / 8), 256, 0, s>>>(
+        stats, reinterpret_cast<const long long*>(targets), static_cast<int>(n_tokens),
+        static_cast<int>(n_grad), acc, acc_scale, reinterpret_cast<const __half*>(weight),
+        ld_weight, vocab_col0, vocab_cols, static_cast<int>(hidden_size),
+        reinterpret_cast<const long long*>(grad_rows), token_loss, token_entropy, correct,
+        head::GradDest{nullptr, 1, reinterpret_cast<const unsigned long long*>(peers), L.recv,
+                       L.rpr, static_cast<int>(rank), n_grad, 0},
+        1, L, static_cast<int>(world), epoch);
+    st = check_launch("head finalize kernel (per-row outputs)");
+    if (st != TALM_OK) return st;
+  }
+  head::ScatterParams sc{};
+  sc.on = 1;
+  // the ranks start on different owners: rank r on the tiles of the rows rank r + 1 owns
+  const int64_t n_h_tiles = (hidden_size + head::BN - 1) / head::BN;
+  const int64_t n_pair_rows = (n_grad + head::PAIR_ROWS - 1) / head::PAIR_ROWS;
+  sc.tile_shift = static_cast<int>(
+      ((((rank + 1) % world) * L.rpr / head::PAIR_ROWS) % n_pair_rows) * n_h_tiles);
+  sc.acc = acc;
+  sc.scale = acc_scale;
+  sc.targets = reinterpret_cast<const long long*>(targets);
+  sc.grad_rows = reinterpret_cast<const long long*>(grad_rows);
+  sc.weight = reinterpret_cast<const __half*>(weight);
+  sc.ld_weight = ld_weight;
+  sc.col0 = vocab_col0;
+  sc.vcols = vocab_cols;
+  sc.peers = reinterpret_cast<const unsigned long long*>(peers);
+  sc.L = L;
+  sc.rank = static_cast<int>(rank);
+  sc.world = static_cast<int>(world);
+  sc.epoch = epoch;
+  return head::shard_walk(nullptr, hidden_size, weight, ld_weight, targets, n_tokens, n_grad,
+                          hidden_size, vocab_cols, vocab_col0, vocab_chunk,
+                          const_cast<float*>(stats), acc, workspace, ws_bytes, s,
+                          head::WALK_LAST, &sc);
 }
 
 int talm_head_finalize(const float* stats, const int64_t* targets, int64_t n_tokens,
@@ -1335,7 +1541,7 @@ int talm_head_finalize_scatter(const float* stats, const int64_t* targets, int64
       ld_weight, vocab_col0, vocab_cols, static_cast<int>(hidden_size),
       reinterpret_cast<const long long*>(grad_rows), token_loss, token_entropy, correct,
       head::GradDest{nullptr, 1, reinterpret_cast<const unsigned long long*>(peers), L.recv,
-                     L.rpr, static_cast<int>(rank)},
+                     L.rpr, static_cast<int>(rank), 0, 1},
       vec4, L, static_cast<int>(world), epoch);
   return check_launch("head finalize scatter kernel");
 }

@@ -46,7 +46,12 @@ def shard_bounds(vocab, world, rank):
 class CudaHeadOps:
     """The three kernel steps of the sharded head through the C ABI."""
 
-    def shard(self, h16, w16, ld_w, targets, n_grad, hidden_cols, col0, vocab_chunk):
+    def shard(self, h16, w16, ld_w, targets, n_grad, hidden_cols, col0, vocab_chunk,
+              begin=False):
+        """The walk over this rank's rows: (stats, acc). With `begin`, every step but the last
+        accumulator GEMM (talm_head_shard_begin), and the workspace is returned as well: the
+        peer flow finishes the walk with talm_head_shard_finish_scatter once the statistics
+        are merged."""
         lib = _lib.load()
         device = h16.device
         n_tokens, cols = h16.shape[0], w16.shape[0]
@@ -58,11 +63,12 @@ class CudaHeadOps:
         _lib.check(lib.talm_head_workspace_size(n_tokens, n_grad, hidden_cols, cols, vocab_chunk,
                                                 size), "talm_head_workspace_size")
         ws = torch.empty(size.value, dtype=torch.uint8, device=device)
-        _lib.check(lib.talm_head_shard(_lib.ptr(h16), h16.stride(0), _lib.ptr(w16), ld_w,
-                                       _lib.ptr(targets), n_tokens, n_grad, hidden_cols, cols,
-                                       col0, vocab_chunk, _lib.ptr(stats), _lib.ptr(acc),
-                                       _lib.ptr(ws), size.value, stream), "talm_head_shard")
-        return stats, acc
+        fn, name = ((lib.talm_head_shard_begin, "talm_head_shard_begin") if begin
+                    else (lib.talm_head_shard, "talm_head_shard"))
+        _lib.check(fn(_lib.ptr(h16), h16.stride(0), _lib.ptr(w16), ld_w, _lib.ptr(targets),
+                      n_tokens, n_grad, hidden_cols, cols, col0, vocab_chunk, _lib.ptr(stats),
+                      _lib.ptr(acc), _lib.ptr(ws), size.value, stream), name)
+        return (stats, acc, ws) if begin else (stats, acc)
 
     def combine(self, gathered, rank, n_grad):
         lib = _lib.load()
@@ -96,6 +102,10 @@ class CudaHeadOps:
 OPS = CudaHeadOps()
 
 PEER_EXCHANGE = os.environ.get("TALM_B200_PEER_EXCHANGE", "1") != "0"
+# Under the peer exchange, the walk's last accumulator GEMM finishes the gradient rows and
+# stores them at their owners from its epilogue (talm_head_shard_finish_scatter), instead of a
+# separate finalize pass over acc after it; 0 keeps the separate pass.
+FUSED_SCATTER = os.environ.get("TALM_B200_FUSED_SCATTER", "1") != "0"
 
 
 class PeerExchange:
@@ -180,9 +190,12 @@ def _exchange(group, device, n_tokens, hidden_cols):
     return ex if ex.ensure(n_tokens, hidden_cols) else None
 
 
-def _peer_flow(ex, stats, acc, rows_targets, n_grad, w16, ld_w, col0, cols, src, need_grad):
+def _peer_flow(ex, stats, acc, rows_targets, n_grad, w16, ld_w, col0, cols, src, need_grad,
+               walk=None):
     """Steps 2-5 through the peer buffers: returns token_loss, token_entropy, correct (int32)
-    and the reduced fp16 gradient [N, cols] (or None)."""
+    and the reduced fp16 gradient [N, cols] (or None). `walk` = (workspace, vocab_chunk) of a
+    walk run by talm_head_shard_begin: its last accumulator GEMM then runs here, after the
+    merge, and scatters the finished gradient rows itself."""
     lib = _lib.load()
     device = stats.device
     stream = _lib.stream_of(device)
@@ -205,11 +218,20 @@ def _peer_flow(ex, stats, acc, rows_targets, n_grad, w16, ld_w, col0, cols, src,
             ld_w, col0, w16.shape[0], cols, _lib.ptr(src), _lib.ptr(token_loss),
             _lib.ptr(token_entropy), _lib.ptr(correct), None, 0, stream), "talm_head_finalize")
         return token_loss, token_entropy, correct, None
-    _lib.check(lib.talm_head_finalize_scatter(
-        _lib.ptr(merged), _lib.ptr(rows_targets), n_tokens, n_grad, _lib.ptr(acc),
-        _lib.ptr(scale), _lib.ptr(w16), ld_w, col0, w16.shape[0], cols, _lib.ptr(src),
-        _lib.ptr(token_loss), _lib.ptr(token_entropy), _lib.ptr(correct), ex.rank, ex.world,
-        peers, epoch, stream), "talm_head_finalize_scatter")
+    if walk is not None:
+        ws, vocab_chunk = walk
+        _lib.check(lib.talm_head_shard_finish_scatter(
+            _lib.ptr(w16), ld_w, _lib.ptr(rows_targets), n_tokens, n_grad, cols, w16.shape[0],
+            col0, vocab_chunk, _lib.ptr(merged), _lib.ptr(acc), _lib.ptr(scale), _lib.ptr(ws),
+            ws.numel(), _lib.ptr(src), _lib.ptr(token_loss), _lib.ptr(token_entropy),
+            _lib.ptr(correct), ex.rank, ex.world, peers, epoch, stream),
+            "talm_head_shard_finish_scatter")
+    else:
+        _lib.check(lib.talm_head_finalize_scatter(
+            _lib.ptr(merged), _lib.ptr(rows_targets), n_tokens, n_grad, _lib.ptr(acc),
+            _lib.ptr(scale), _lib.ptr(w16), ld_w, col0, w16.shape[0], cols, _lib.ptr(src),
+            _lib.ptr(token_loss), _lib.ptr(token_entropy), _lib.ptr(correct), ex.rank, ex.world,
+            peers, epoch, stream), "talm_head_finalize_scatter")
     _lib.check(lib.talm_head_reduce_gather(n_tokens, cols, ex.rank, ex.world, peers, epoch,
                                            stream), "talm_head_reduce_gather")
     grad = torch.empty(n_tokens, cols, dtype=torch.float16, device=device)
@@ -243,13 +265,20 @@ def sharded_head(hidden, weight_shard, targets, vocab, col0, num_items=None, voc
             h16 = h16.index_select(0, src)
             rows_targets = targets.index_select(0, src)
 
-    stats, acc = ops.shard(h16, w16, ld_w, rows_targets, n_grad, cols, col0, int(vocab_chunk))
-    ex = (_exchange(group, stats.device, n_tokens, cols)
+    ex = (_exchange(group, hidden.device, n_tokens, cols)
           if PEER_EXCHANGE and isinstance(ops, CudaHeadOps) and world > 1 and n_tokens > 0
           else None)
+    walk = None
+    if ex is not None and FUSED_SCATTER and need_grad and n_grad > 0:
+        stats, acc, ws = ops.shard(h16, w16, ld_w, rows_targets, n_grad, cols, col0,
+                                   int(vocab_chunk), begin=True)
+        walk = (ws, int(vocab_chunk))
+    else:
+        stats, acc = ops.shard(h16, w16, ld_w, rows_targets, n_grad, cols, col0,
+                               int(vocab_chunk))
     if ex is not None:
         token_loss, token_entropy, correct, grad = _peer_flow(
-            ex, stats, acc, rows_targets, n_grad, w16, ld_w, col0, cols, src, need_grad)
+            ex, stats, acc, rows_targets, n_grad, w16, ld_w, col0, cols, src, need_grad, walk)
         if grad is not None:
             grad = grad[:, :hidden_size]
         denom = _denominator(num_items, labelled.sum())

@@ -1,7 +1,8 @@
 """The vocabulary-parallel head over NCCL on 2+ GPUs (one process per GPU) against the
 single-GPU fused head on the same inputs: identical per-token outputs (up to fp32 merge order),
-the same accuracy, and the gradient within the head's tolerance. Skipped with fewer than 2
-GPUs."""
+the same accuracy, and the gradient within the head's tolerance. The peer flow with the scatter
+inside the walk's last accumulator GEMM must give the same bits as the peer flow with a
+separate finalize pass. Skipped with fewer than 2 GPUs."""
 
 import os
 import socket
@@ -19,12 +20,12 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _case(n, vocab, size, device):
+def _case(n, vocab, size, device, unlabelled=0.4):
     g = torch.Generator(device=device).manual_seed(31)
     hidden = torch.randn(n, size, generator=g, device=device).half()
     weight = (torch.randn(vocab, size, generator=g, device=device) * 0.05).half()
     targets = torch.randint(0, vocab, (n,), generator=g, device=device)
-    targets[torch.rand(n, generator=g, device=device) < 0.4] = -100
+    targets[torch.rand(n, generator=g, device=device) < unlabelled] = -100
     hidden[1] = (weight[vocab - 3].float() * 30).half()   # a confident row in the last shard
     targets[1] = vocab - 3
     return hidden, weight, targets
@@ -47,19 +48,27 @@ def _worker(rank, world, port, q, sizes, vocab, size, flow):
 
         vocab_parallel.PEER_EXCHANGE = flow != "nccl"
         col0, cols = shard_bounds(vocab, world, rank)
-        results = []
-        # several calls: the peer buffers are reused (epochs) and grow once (600 -> 1500 rows)
-        for n in sizes:
-            hidden, weight, targets = _case(n, vocab, size, dev)
+
+        def sharded(hidden, weight, targets, fused):
+            vocab_parallel.FUSED_SCATTER = fused
             x = hidden.clone().requires_grad_(True)
             out = vocab_parallel_head_loss(x, weight[col0:col0 + cols], targets, vocab, col0,
                                            None, 2048)
             (out[0] * 7.0).backward()
+            return [t.detach().cpu() for t in out], x.grad.cpu()
+
+        results = []
+        # several calls: the peer buffers are reused (epochs) and grow once (600 -> 1500 rows);
+        # partly labelled rows (compacted), every row labelled, and a single labelled row
+        for n, unlabelled in sizes:
+            hidden, weight, targets = _case(n, vocab, size, dev, unlabelled)
+            out, grad = sharded(hidden, weight, targets, True)
+            # the same exchange with a separate finalize pass (peer flow only)
+            split = sharded(hidden, weight, targets, False) if flow == "peer" else None
             y = hidden.clone().requires_grad_(True)
             ref = fused_head_loss(y, weight, targets, None, 2048)
             (ref[0] * 7.0).backward()
-            results.append(([t.detach().cpu() for t in out], x.grad.cpu(),
-                            [t.detach().cpu() for t in ref], y.grad.cpu()))
+            results.append((out, grad, [t.detach().cpu() for t in ref], y.grad.cpu(), split))
         from talm_b200 import _lib
         q.put((rank, results, _lib.device_status()))
         dist.barrier()
@@ -73,7 +82,7 @@ def test_vocab_parallel_matches_single_gpu(flow):
     world = torch.cuda.device_count()
     if world < 2:
         pytest.skip("needs 2 or more GPUs")
-    sizes, vocab, size = (600, 1500, 600), 30011, 512
+    sizes, vocab, size = ((600, 0.4), (1500, 0.0), (600, 0.4), (300, 1.0)), 30011, 512
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -87,7 +96,10 @@ def test_vocab_parallel_matches_single_gpu(flow):
         assert p.exitcode == 0
     for rank, calls, status in results:
         assert status == 0, f"rank {rank}: device status {status}"
-        for out, grad, ref, ref_grad in calls:
+        for out, grad, ref, ref_grad, split in calls:
+            if split is not None:  # scatter in the last accumulator GEMM: the same bits
+                for a, b in zip(out + [grad], split[0] + [split[1]]):
+                    assert torch.equal(a, b), f"rank {rank}: fused scatter differs"
             loss, token_loss, entropy, correct = out
             r_loss, r_tl, r_ent, r_corr = ref
             torch.testing.assert_close(loss, r_loss, rtol=1e-5, atol=1e-6)
