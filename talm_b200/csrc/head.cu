@@ -710,55 +710,63 @@ __global__ void __launch_bounds__(SLICE_THREADS, 1)
           }
         }
       } else if (p.sc.on) {  // the walk's last accumulator step: finish the rows, send them
+        // Per 32-column chunk: D (one row per thread, as TMEM gives it) goes through the
+        // group's staging buffer, then 8 lanes per row (4 columns each) finish 4 rows per
+        // step, so that every row piece leaves as one 128-byte line (a store of a lane per row
+        // would split each line into 16-byte writes over NVLink).
         const ScatterParams& sc = p.sc;
         const int ht = unit.tile % ap.n_h_tiles, pr = unit.tile / ap.n_h_tiles;
-        const int row = pr * PAIR_ROWS + static_cast<int>(rank) * BM + r_in_tile;
+        const int row0 = pr * PAIR_ROWS + static_cast<int>(rank) * BM;
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-        const bool valid = row < ap.n_grad;
-        const long long tgt = valid ? sc.targets[row] : -1;
-        const bool live = tgt >= 0;
-        const bool own = live && tgt >= sc.col0 && tgt < sc.col0 + sc.vcols;
-        const float scale = live ? sc.scale[row] : 0.0f;
-        const long long out = valid ? (sc.grad_rows ? sc.grad_rows[row] : row) : 0;
-        const long long owner = out / sc.L.rpr;
-        float* const dst =
-            reinterpret_cast<float*>(sc.peers[valid ? owner : sc.rank] + sc.L.recv) +
-            (static_cast<long long>(sc.rank) * sc.L.rpr + (out - owner * sc.L.rpr)) * ap.hidden;
-        const float* const arow = sc.acc + static_cast<long long>(valid ? row : 0) * ap.hidden;
-        const __half* const wrow = sc.weight + (own ? (tgt - sc.col0) * sc.ld_weight : 0);
+        uint8_t* const buf = bufs;
+        const int sub = lane >> 3, piece = lane & 7;
   #pragma unroll 1
         for (int c = g * (EPI_COLS / 32); c < (g + 1) * (EPI_COLS / 32); ++c) {
-          const int h0 = ht * BN + c * 32;
           uint32_t r[32];
           tmem_ld_32x32b_x32(taddr + c * 32, r);
-          // the earlier slices' sums load while the TMEM load is in flight
-          float4 a[8];
+          tmem_wait_ld();
   #pragma unroll
           for (int v = 0; v < 8; ++v)
-            a[v] = (valid && h0 + 4 * v < ap.hidden)
-                       ? *reinterpret_cast<const float4*>(arow + h0 + 4 * v)
-                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-          tmem_wait_ld();
-          if (!valid) continue;
-  #pragma unroll
-          for (int v = 0; v < 8; ++v) {
-            const int h = h0 + 4 * v;
-            if (h >= ap.hidden) break;
-            float w[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            if (own) {
-              const uint2 wv = *reinterpret_cast<const uint2*>(wrow + h);
-              const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
-              const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
-              w[0] = w01.x; w[1] = w01.y; w[2] = w23.x; w[3] = w23.y;
+            stage_chunk(buf, r_in_tile, v, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+          named_barrier(bar_id, EPI_THREADS);
+          const int h = ht * BN + c * 32 + piece * 4;
+          if (h < ap.hidden) {
+  #pragma unroll 2
+            for (int i = 0; i < 8; ++i) {
+              const int rl = q * 32 + i * 4 + sub;  // the tile row (of this CTA's 128)
+              const int row = row0 + rl;
+              if (row >= ap.n_grad) continue;
+              const long long tgt = sc.targets[row];
+              const bool live = tgt >= 0;
+              const bool own = live && tgt >= sc.col0 && tgt < sc.col0 + sc.vcols;
+              const float scale = live ? sc.scale[row] : 0.0f;
+              const long long out = sc.grad_rows ? sc.grad_rows[row] : row;
+              const long long owner = out / sc.L.rpr;
+              float* const dst =
+                  reinterpret_cast<float*>(sc.peers[owner] + sc.L.recv) +
+                  (static_cast<long long>(sc.rank) * sc.L.rpr + (out - owner * sc.L.rpr)) *
+                      ap.hidden + h;
+              const float4 a =
+                  *reinterpret_cast<const float4*>(sc.acc + static_cast<long long>(row) * ap.hidden + h);
+              const uint4 d =
+                  *reinterpret_cast<const uint4*>(buf + rl * 128 + ((piece ^ (rl & 7)) << 4));
+              float w[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+              if (own) {
+                const uint2 wv = *reinterpret_cast<const uint2*>(
+                    sc.weight + (tgt - sc.col0) * sc.ld_weight + h);
+                const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
+                const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
+                w[0] = w01.x; w[1] = w01.y; w[2] = w23.x; w[3] = w23.y;
+              }
+              // acc + D as the reduce-add of the other steps forms it, then the finalize
+              *reinterpret_cast<float4*>(dst) = make_float4(
+                  grad_value(live, own, __fadd_rn(a.x, __uint_as_float(d.x)), scale, w[0]),
+                  grad_value(live, own, __fadd_rn(a.y, __uint_as_float(d.y)), scale, w[1]),
+                  grad_value(live, own, __fadd_rn(a.z, __uint_as_float(d.z)), scale, w[2]),
+                  grad_value(live, own, __fadd_rn(a.w, __uint_as_float(d.w)), scale, w[3]));
             }
-            // acc + D as the reduce-add of the other steps forms it, then the finalize
-            const float4 o = make_float4(
-                grad_value(live, own, __fadd_rn(a[v].x, __uint_as_float(r[4 * v])), scale, w[0]),
-                grad_value(live, own, __fadd_rn(a[v].y, __uint_as_float(r[4 * v + 1])), scale, w[1]),
-                grad_value(live, own, __fadd_rn(a[v].z, __uint_as_float(r[4 * v + 2])), scale, w[2]),
-                grad_value(live, own, __fadd_rn(a[v].w, __uint_as_float(r[4 * v + 3])), scale, w[3]));
-            *reinterpret_cast<float4*>(dst + h) = o;
           }
+          named_barrier(bar_id, EPI_THREADS);  // read out before the next chunk refills it
         }
         tc_fence_before();
         __syncwarp();
