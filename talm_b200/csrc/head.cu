@@ -605,12 +605,11 @@ __global__ void __launch_bounds__(SLICE_THREADS, 1)
         // probabilities (written to `buf`, 16-byte chunks qbase..qbase+3 of this row). The TMEM
         // load is warp-collective (.sync.aligned): every lane executes it. `full` (a compile-time
         // flag: the group's columns are all valid) drops the per-column bounds tests.
-        auto chunk = [&](auto full, int c, bool track, bool sum, float mscaled, uint8_t* buf,
-                         int qbase) {
+        uint32_t packed[16];  // the last chunk's probabilities, fp16 pairs
+        auto chunk = [&](auto full, int c, bool track, bool sum, float mscaled) {
           constexpr bool kFull = decltype(full)::value;
           tmem_ld_32x32b_x32(taddr + c * 32, r);
           tmem_wait_ld();
-          uint32_t packed[16];
   #pragma unroll
           for (int j = 0; j < 32; j += 2) {
             const int col = c * 32 + j;
@@ -636,30 +635,35 @@ __global__ void __launch_bounds__(SLICE_THREADS, 1)
               packed[j / 2] = pack_half2(e0, e1);
             }
           }
-          if (sum && buf != nullptr) {
+        };
+        // the last chunk's probabilities into 16-byte pieces qbase..qbase+3 of this row
+        auto stage = [&](uint8_t* buf, int qbase) {
   #pragma unroll
-            for (int v = 0; v < 4; ++v)
-              stage_chunk(buf, r_in_tile, qbase + v, packed[4 * v], packed[4 * v + 1],
-                          packed[4 * v + 2], packed[4 * v + 3]);
-          }
+          for (int v = 0; v < 4; ++v)
+            stage_chunk(buf, r_in_tile, qbase + v, packed[4 * v], packed[4 * v + 1],
+                        packed[4 * v + 2], packed[4 * v + 3]);
         };
         // A pass with sums over the group's columns: 2 blocks of 64 columns, each staged and
-        // stored. `base` per lane; `track` for the single-pass case.
+        // stored. `base` per lane; `track` for the single-pass case. The first chunk of a block
+        // is loaded and computed before the wait for the staging buffer (the previous block's
+        // store may still be reading it), so that the wait overlaps that work.
         auto sum_pass = [&](auto full, bool track, float base) {
           const float mscaled = base * kLog2e;
   #pragma unroll 1
           for (int kb = g * (EPI_COLS / 64); kb < (g + 1) * (EPI_COLS / 64); ++kb) {
             uint8_t* buf = bufs + nb * 16384;
+            chunk(full, 2 * kb, track, true, mscaled);
             if (store_p) {
               // the store issued from this buffer two blocks ago has read it (at most the last
               // store, from the other buffer, may still be reading)
               if (elected) bulk_wait_read<STAGING_PER_GROUP - 1>();
               named_barrier(bar_id, EPI_THREADS);
               nb = (nb + 1) % STAGING_PER_GROUP;
+              stage(buf, 0);
             }
-            chunk(full, 2 * kb, track, true, mscaled, store_p ? buf : nullptr, 0);
-            chunk(full, 2 * kb + 1, track, true, mscaled, store_p ? buf : nullptr, 4);
+            chunk(full, 2 * kb + 1, track, true, mscaled);
             if (store_p) {
+              stage(buf, 4);
               fence_proxy_async_smem();
               named_barrier(bar_id, EPI_THREADS);
               if (elected) {
@@ -688,7 +692,7 @@ __global__ void __launch_bounds__(SLICE_THREADS, 1)
           } else {
   #pragma unroll 1
             for (int c = g * (EPI_COLS / 32); c < (g + 1) * (EPI_COLS / 32); ++c)
-              chunk(full, c, true, false, 0.0f, nullptr, 0);
+              chunk(full, c, true, false, 0.0f);
             sum_pass(full, false, mx);
           }
         };
