@@ -93,9 +93,8 @@ def labelled_first_rows(h16, targets, n_labelled):
     """Device-side labelled-first compaction (talm_head_labelled_first): the fp16 rows and
     their targets in the order of `labelled_first`, and `src` (the input row of each position),
     in two launches instead of labelled_first + two index_select. h16: [N, cols] fp16 rows of
-    16-byte multiples on 16-byte boundaries; n_labelled: the exact count of targets >= 0.
-    (FusedHeadLossVocab keeps the reference's torch ops for this step: measured on config 2,
-    the device version did not make the step faster.)"""
+    16-byte multiples on 16-byte boundaries; n_labelled: the exact count of targets >= 0 (a
+    count that does not match records TALM_ERANGE in the device status word)."""
     lib = _lib.load()
     n, cols = h16.shape
     src = torch.empty(n, dtype=torch.int64, device=h16.device)
@@ -183,17 +182,16 @@ class FusedHeadLossVocab(torch.autograd.Function):
         h16, _ = _operand(hidden.detach().to(torch.float16), cols)
         w16, ld_w = _operand(weight.detach(), cols)
         targets = targets.contiguous().to(torch.int64)
-        labelled = targets >= 0
 
         n_grad, src, rows_targets = (n_tokens if need_grad else 0), None, targets
         if need_grad and COMPACT and n_tokens > 0:
             if n_labelled is None:
-                n_labelled = int(labelled.sum())
+                n_labelled = int((targets >= 0).sum())
             n_grad = int(n_labelled)
             if 0 < n_grad < n_tokens:
-                _dest, src = labelled_first(labelled, n_grad)
-                h16 = h16.index_select(0, src)
-                rows_targets = targets.index_select(0, src)
+                # the order of labelled_first, built on the device in two launches
+                # (talm_head_labelled_first) instead of ten torch ops
+                h16, rows_targets, src = labelled_first_rows(h16, targets, n_grad)
                 RAN["compact"] += 1
 
         if n_tokens > 0:
@@ -208,7 +206,13 @@ class FusedHeadLossVocab(torch.autograd.Function):
         if need_grad and cols != hidden_size:
             grad = grad[:, :hidden_size]
 
-        denom = _denominator(num_items, labelled.sum())
+        if num_items is None and n_labelled is not None:
+            # the labelled count is known on the host: the reference's denominator
+            # (count clamped to 1, fp32) in one fill instead of a device count
+            denom = torch.full((), float(max(int(n_labelled), 1)), dtype=torch.float32,
+                               device=hidden.device)
+        else:
+            denom = _denominator(num_items, (targets >= 0).sum())
         loss = token_loss.sum() / denom
         correct = correct.to(torch.bool)
         ctx.denom = denom
