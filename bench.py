@@ -17,7 +17,7 @@ Same line, secondary objects:
        double-quantised absmax, one grouped launch per layer, layers sharded over the ranks)
   e2e  the headline through the same API with host buffers: pinned-host -> device copies of the
        step's hidden states and labels and the device -> host read of the loss inside the timed
-       region
+       region (each step's copy of the next step's inputs overlaps its kernels)
   roofline     the dominant kernel (head_slice_kernel) against the measured bf16/fp16 peak
   cpu_baseline the CPU oracle (a restatement of the reference's torch formula,
                solution/test_kernels.py:70-83) on a bounded sample, rank 0, N=1
@@ -539,7 +539,10 @@ def run_head_e2e(world, rank, steps, warmup, hidden, weight, targets):
     """Public API with host buffers: H2D of the step's hidden states + labels, D2H of the loss.
     At N > 1 each rank copies its 1/N of the hidden rows from pinned host memory and the ranks
     all-gather them over NVLink (NCCL), instead of N full host copies; the labels (8 B a row)
-    are copied whole by every rank."""
+    are copied whole by every rank. As a training loop's input pipeline does, the copy of the
+    next step's inputs runs on a copy stream into the other of two device buffers while this
+    step computes; every step still waits for that copy before it reads its loss back, so each
+    timed step holds one whole input copy and one loss read."""
     from talm_b200.fused_head import fused_head_loss
     from talm_b200.vocab_parallel import shard_bounds, vocab_parallel_head_loss
 
@@ -552,22 +555,47 @@ def run_head_e2e(world, rank, steps, warmup, hidden, weight, targets):
     col0 = shard_bounds(VOCAB, world, rank)[0] if world > 1 else 0
     full = torch.empty_like(hidden) if equal else None
     sink = []
+    copy_stream = torch.cuda.Stream()
+    bufs = [(torch.empty(h_host.shape, dtype=h_host.dtype, device="cuda"),
+             torch.empty(t_host.shape, dtype=t_host.dtype, device="cuda")) for _ in range(2)]
+    ready = [torch.cuda.Event(), torch.cuda.Event()]
+    free = [torch.cuda.Event(), torch.cuda.Event()]
+    for e in free:
+        e.record()
+    state = {"i": 0}
+
+    def issue_copy(j):
+        b = j % 2
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(free[b])  # the step that read this buffer is done with it
+            bufs[b][0].copy_(h_host, non_blocking=True)
+            bufs[b][1].copy_(t_host, non_blocking=True)
+            ready[b].record(copy_stream)
 
     def step():
-        part = h_host.to("cuda", non_blocking=True)
+        i = state["i"]
+        b = i % 2
+        if i == 0:
+            issue_copy(0)
+        issue_copy(i + 1)  # the next step's inputs, beside this step's kernels
+        torch.cuda.current_stream().wait_event(ready[b])
+        part, t = bufs[b]
         if equal:
             dist.all_gather_into_tensor(full, part)
             h = full.detach().requires_grad_(True)
         else:
-            h = part.requires_grad_(True)
-        t = t_host.to("cuda", non_blocking=True)
+            h = part.detach().requires_grad_(True)
         if world == 1:
             loss, *_ = fused_head_loss(h, weight, t, None, CHUNK, n_labelled=n_lab)
         else:
             loss, *_ = vocab_parallel_head_loss(h, weight, t, VOCAB, col0, None, CHUNK,
                                                 n_labelled=n_lab)
         loss.backward()
+        free[b].record()
+        # the next step's copy is part of this step: it has landed before the loss is read
+        torch.cuda.current_stream().wait_event(ready[(i + 1) % 2])
         sink.append(loss.item())
+        state["i"] = i + 1
 
     for _ in range(warmup):
         step()
@@ -794,7 +822,10 @@ def ours(args, world, rank, local):
                      "step_TFLOPs": head_flops(n_tok, n_lab) / (head["ms_per_step"] / 1000)
                      / 1e12},
         "e2e": {"value": n_tok / (e2e_ms / 1000), "unit": "tokens/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "input_pipeline": "each step's kernels run beside the pinned-host copy of the "
+                                  "next step's inputs (copy stream, two device buffers); the step "
+                                  "waits for that copy and reads its loss back before it ends"},
         "gpu_launches": int(sum(v[1] for v in kernels.values()) / max(args.steps, 1)
                             * args.steps * world),
         "clocks": head["clocks"],
