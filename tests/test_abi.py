@@ -135,3 +135,25 @@ def test_fused_nf4_gemm_rejects_bad_arguments(lib):
     assert call(n_rows=-1) == 1
     assert call(n_rows=0) == 0                   # nothing to do: no pointer read
     assert b"qblock" in (call(qblock=32) and lib.talm_last_error())
+
+
+def test_split_walk_rejects_bad_arguments(lib):
+    """talm_head_shard_begin / talm_head_shard_finish_scatter validate sizes and the rank
+    before they touch a pointer or the device."""
+    # the walk's first part: n_grad above n_tokens, hidden not a multiple of 8
+    assert lib.talm_head_shard_begin(None, 8, None, 8, None, 4, 5, 8, 100, 0, 64, None, None,
+                                     None, 0, None) == 1
+    assert lib.talm_head_shard_begin(None, 12, None, 12, None, 4, 4, 12, 100, 0, 64, None,
+                                     None, None, 0, None) == 1
+    assert lib.talm_head_shard_begin(None, 8, None, 8, None, 0, 0, 8, 100, 0, 64, None, None,
+                                     None, 0, None) == 0     # no rows: nothing to do
+
+    def finish(n=4, n_grad=2, hidden=8, rank=0, world=2, acc=None):
+        return lib.talm_head_shard_finish_scatter(None, 8, None, n, n_grad, hidden, 100, 0, 64,
+                                                  None, acc, None, None, 0, None, None, None,
+                                                  None, rank, world, None, 1, None)
+    assert finish(n_grad=5) == 1                 # more gradient rows than rows
+    assert finish(rank=2) == 1                   # rank outside the group
+    assert finish(hidden=12) == 1                # hidden columns: multiples of 8
+    assert finish() == 1                         # null peer table, statistics and acc
+    assert b"null" in lib.talm_last_error()
