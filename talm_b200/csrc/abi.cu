@@ -138,6 +138,26 @@ int talm_make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t inner, ui
                       row_stride_elems, box_inner, box_outer);
 }
 
+int talm_make_tmap_kchunks_f16(CUtensorMap* map, const void* base, uint64_t k, uint64_t rows,
+                               uint64_t row_stride_elems, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return talm::set_error(TALM_ENODEV, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (row_stride_elems * 2) % 16 != 0 ||
+      k % 64 != 0)
+    return talm::set_error(TALM_EINVAL, "k-chunk tensor map: base, row stride or k (%llu)",
+                           (unsigned long long)k);
+  cuuint64_t dims[3] = {64, rows, k / 64};
+  cuuint64_t strides[2] = {row_stride_elems * 2, 128};
+  cuuint32_t box[3] = {64, box_rows, 2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return talm::set_error(TALM_EINVAL, "cuTensorMapEncodeTiled (k chunks) failed (%d)", (int)r);
+  return TALM_OK;
+}
+
 static int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, uint64_t elem_bytes,
                         const void* base, uint64_t inner, uint64_t outer,
                         uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,

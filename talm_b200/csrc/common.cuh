@@ -320,6 +320,16 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map,
+                                                 uint32_t bar_cluster, int32_t c0, int32_t c1,
+                                                 int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                    smem_u32(dst_smem)),
@@ -390,3 +400,8 @@ int talm_make_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t inner, ui
                           uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer);
 int talm_make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                           uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer);
+// Host: a row-major fp16 [rows][k] matrix (k % 64 == 0) as a 3-D tensor map {64, rows, k / 64}
+// (128-byte swizzle) whose box {64, box_rows, 2} is two consecutive 64-column chunks of
+// box_rows rows: one request fills two 128-byte-swizzled tiles of box_rows rows, back to back.
+int talm_make_tmap_kchunks_f16(CUtensorMap* map, const void* base, uint64_t k, uint64_t rows,
+                               uint64_t row_stride_elems, uint32_t box_rows);

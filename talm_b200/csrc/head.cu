@@ -183,6 +183,7 @@ struct LogitsParams {
   int n_parts;        // n_col_tiles * PARTS: statistics records per row
   int n_pair_rows;    // ceil(n_tokens / PAIR_ROWS)
   int band_rows;      // pair rows per band of the tile order (logits_tile)
+  int k3d;            // stages of two sub-blocks load through the 3-D k-chunk maps
   long long col_base; // global column id of slice column 0
   int has_ref;        // 0 on the first slice: no reference yet
   const long long* targets;
@@ -322,6 +323,7 @@ struct AccumParams {
   int slice_row0;    // first weight row of the slice
   int n_pair_rows;   // ceil(n_grad / PAIR_ROWS)
   int n_h_tiles;     // ceil(hidden / BN)
+  int k3d;           // stages load through the 3-D k-chunk maps (hidden % 64 == 0)
 };
 
 // ------------------------------------------------------------------------------------------
@@ -446,7 +448,10 @@ __global__ void __launch_bounds__(SLICE_THREADS, 1)
                       const __grid_constant__ CUtensorMap tm_probs_out,
                       const __grid_constant__ CUtensorMap tm_probs_in,
                       const __grid_constant__ CUtensorMap tm_weight_mn,
-                      const __grid_constant__ CUtensorMap tm_acc, SliceParams p) {
+                      const __grid_constant__ CUtensorMap tm_acc,
+                      const __grid_constant__ CUtensorMap tm_hidden3,
+                      const __grid_constant__ CUtensorMap tm_weight3,
+                      const __grid_constant__ CUtensorMap tm_probs3_in, SliceParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = aligned_smem(smem_raw);
   uint8_t* staging = smem + STAGES * STAGE_BYTES;
@@ -487,6 +492,24 @@ __global__ void __launch_bounds__(SLICE_THREADS, 1)
           if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort)) break;
           const uint32_t lfull = mapa_shared(smem_u32(&ctl->full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&ctl->full[stage], 2 * nsub * SUB_BYTES);
+          uint8_t* const st = smem + stage * STAGE_BYTES;
+          if (nsub == 2 && (unit.type == 0 ? lp.k3d : ap.k3d)) {
+            // one request per operand for both sub-blocks (3-D k-chunk boxes): the stage
+            // holds A0 A1 B0 B1 (logits) or A0 A1 and the two 64-column weight groups of
+            // 128 K-rows each (accumulator); TMA requests, not bytes, limit the operand feed
+            if (unit.type == 0) {
+              int pr, ct;
+              logits_tile(lp, unit.tile, pr, ct);
+              tma_load_3d_pair(st, &tm_hidden3, lfull, 0, pr * PAIR_ROWS + rank * BM, kb0);
+              tma_load_3d_pair(st + 2 * A_BYTES, &tm_weight3, lfull, 0,
+                               lp.slice_row0 + ct * BN + rank * (BN / 2), kb0);
+            } else {
+              const int ht = unit.tile % ap.n_h_tiles, pr = unit.tile / ap.n_h_tiles;
+              tma_load_3d_pair(st, &tm_probs3_in, lfull, 0, pr * PAIR_ROWS + rank * BM, kb0);
+              tma_load_3d_pair(st + 2 * A_BYTES, &tm_weight3, lfull, 0,
+                               ap.slice_row0 + kb0 * BK, (ht * BN + rank * (BN / 2)) / 64);
+            }
+          } else
           for (int j = 0; j < nsub; ++j) {
             const int kb = kb0 + j;
             uint8_t* a = smem + stage * STAGE_BYTES + j * SUB_BYTES;
@@ -524,9 +547,15 @@ __global__ void __launch_bounds__(SLICE_THREADS, 1)
           const int nsub = min(KSUB, unit.kb1 - kb0);
           if (!mbar_wait(&ctl->full[stage], phase, abort)) { ok = false; break; }
           tc_fence_after();
+          const bool s3 = nsub == 2 && (unit.type == 0 ? lp.k3d : ap.k3d);
+          const uint32_t st = smem_u32(smem + stage * STAGE_BYTES);
           for (int j = 0; j < nsub; ++j) {
-            const uint32_t a = smem_u32(smem + stage * STAGE_BYTES + j * SUB_BYTES);
-            const uint32_t b = a + A_BYTES;
+            const uint32_t a = s3 ? st + j * A_BYTES : st + j * SUB_BYTES;
+            // 3-D stages: B0 B1 after A0 A1 (logits); the accumulator's weight groups of 128
+            // K-rows each, 16 KiB apart, sub-block j at +8 KiB
+            const uint32_t b = s3 ? st + 2 * A_BYTES + j * (unit.type == 0 ? B_BYTES : 64 * BK * 2)
+                                  : a + A_BYTES;
+            const uint32_t lbo_acc = s3 ? 2 * 64 * BK * 2 : 64 * BK * 2;
             const bool first_kb = kb0 + j == unit.kb0;
             if (unit.type == 0) {
 #pragma unroll
@@ -540,7 +569,7 @@ __global__ void __launch_bounds__(SLICE_THREADS, 1)
                 // A: K-major rows of 128 B, +32 B per 16 K. B: MN-major, two 64-wide hidden
                 // groups of BK rows x 128 B (LBO = 8 KiB), 16 K-rows = +2 KiB.
                 umma_f16_pair(d, smem_desc_sw128(a + k * 32, 16, 1024),
-                              smem_desc_sw128(b + k * 2048, 64 * BK * 2, 1024), kIdescAccum,
+                              smem_desc_sw128(b + k * 2048, lbo_acc, 1024), kIdescAccum,
                               !first_kb || k != 0);
             }
           }
@@ -1207,7 +1236,9 @@ int set_attrs() {
 int launch_slice_step(const CUtensorMap& tm_hidden, const CUtensorMap& tm_weight,
                       const CUtensorMap& tm_probs_out, const CUtensorMap& tm_probs_in,
                       const CUtensorMap& tm_weight_mn, const CUtensorMap& tm_acc,
-                      const SliceParams& sp, cudaStream_t stream, int max_pairs) {
+                      const CUtensorMap& tm_hidden3, const CUtensorMap& tm_weight3,
+                      const CUtensorMap& tm_probs3_in, const SliceParams& sp,
+                      cudaStream_t stream, int max_pairs) {
   // one pair per tile at most
   const long long want = static_cast<long long>(sp.n_tiles_l) + sp.n_tiles_a;
   const int pairs = static_cast<int>(std::max(1LL, std::min<long long>(want, max_pairs)));
@@ -1226,7 +1257,8 @@ int launch_slice_step(const CUtensorMap& tm_hidden, const CUtensorMap& tm_weight
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, head_slice_kernel, tm_hidden, tm_weight,
-                                           tm_probs_out, tm_probs_in, tm_weight_mn, tm_acc, sp);
+                                           tm_probs_out, tm_probs_in, tm_weight_mn, tm_acc,
+                                           tm_hidden3, tm_weight3, tm_probs3_in, sp);
   if (e != cudaSuccess) return set_error(TALM_ECUDA, "slice kernel launch: %s", cudaGetErrorString(e));
   return TALM_OK;
 }
@@ -1285,6 +1317,19 @@ int shard_walk(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* weight
     st = talm_make_tmap_2d_f16(&tm_weight_mn, weight, hidden_size, vocab_cols, ld_weight, 64, BK);
   if (st != TALM_OK) return st;
   if (!logits_steps) tm_hidden = tm_weight = tm_weight_mn;  // unused by an accumulator step
+  // 3-D k-chunk maps (two 64-column chunks per request) where the hidden size is a multiple
+  // of 64; the weight map serves the logits tiles (rows = vocabulary rows, chunks along K =
+  // hidden) and the accumulator tiles (rows = K, chunks = hidden column groups) alike
+  const int k3d = hidden_size % 64 == 0 ? 1 : 0;
+  CUtensorMap tm_hidden3 = tm_hidden, tm_weight3 = tm_hidden;
+  if (k3d) {
+    if (logits_steps)
+      st = talm_make_tmap_kchunks_f16(&tm_hidden3, hidden, hidden_size, n_tokens, ld_hidden, BM);
+    if (st == TALM_OK)
+      st = talm_make_tmap_kchunks_f16(&tm_weight3, weight, hidden_size, vocab_cols, ld_weight,
+                                      BN / 2);
+    if (st != TALM_OK) return st;
+  }
   CUtensorMap tm_acc = tm_hidden;
   if (n_grad > 0 && (st = talm_make_tmap_2d_f32(&tm_acc, acc, hidden_size, n_grad, hidden_size,
                                                 32, BM)) != TALM_OK)
@@ -1313,13 +1358,14 @@ int shard_walk(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* weight
   // GEMM of slice k - 1 (its acc rescale needs that) and precedes the one of slice k (which
   // reads the rows it rescales). Steps before k_first are only planned, not launched.
   AccumParams prev_ap{};
-  CUtensorMap prev_tm_probs = tm_hidden;
+  CUtensorMap prev_tm_probs = tm_hidden, prev_tm_probs3 = tm_hidden;
   for (int64_t k = 0; k <= k_last; ++k) {
     const bool run = k >= k_first;
     SliceParams sp{};
     sp.n_tiles_l = 0;
     sp.n_tiles_a = 0;
     CUtensorMap tm_probs_out = tm_hidden;  // unused when no probabilities are stored
+    CUtensorMap tm_probs3 = tm_hidden;     // the same buffer as k chunks, read next step
     int n_col_tiles = 0;
     const int buf = static_cast<int>(k & 1);
     const int64_t s0 = k < n_slices ? sl.begin(k) : 0;
@@ -1337,6 +1383,7 @@ int shard_walk(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* weight
       lp.n_parts = n_col_tiles * PARTS;
       lp.n_pair_rows = n_pair_rows;
       lp.band_rows = std::min(n_pair_rows, kBandRows);
+      lp.k3d = k3d;
       lp.col_base = vocab_col0 + s0;
       lp.has_ref = k != 0;
       lp.targets = reinterpret_cast<const long long*>(targets);
@@ -1345,6 +1392,10 @@ int shard_walk(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* weight
       sp.n_tiles_l = n_pair_rows * n_col_tiles;
       if (n_grad > 0 && (st = talm_make_tmap_2d_f16(&tm_probs_out, ws.probs[buf], chunk, n_grad,
                                                     chunk, 64, BM)) != TALM_OK)
+        return st;
+      if (n_grad > 0 && k3d &&
+          (st = talm_make_tmap_kchunks_f16(&tm_probs3, ws.probs[buf], chunk, n_grad, chunk,
+                                           BM)) != TALM_OK)
         return st;
     }
     if (k >= 1 && n_grad > 0) {
@@ -1355,7 +1406,8 @@ int shard_walk(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* weight
     if (run && sp.n_tiles_l + sp.n_tiles_a > 0) {
       LaunchTimer timer(TALM_KERNEL_HEAD_SLICE, stream);
       st = launch_slice_step(tm_hidden, tm_weight, tm_probs_out, prev_tm_probs, tm_weight_mn,
-                             tm_acc, sp, stream, max_pairs);
+                             tm_acc, tm_hidden3, tm_weight3, prev_tm_probs3, sp, stream,
+                             max_pairs);
       if (st != TALM_OK) return st;
     }
     if (k == n_slices) break;
@@ -1386,7 +1438,9 @@ int shard_walk(const uint16_t* hidden, int64_t ld_hidden, const uint16_t* weight
     prev_ap.slice_row0 = static_cast<int>(s0);
     prev_ap.n_pair_rows = static_cast<int>((n_grad + PAIR_ROWS - 1) / PAIR_ROWS);
     prev_ap.n_h_tiles = static_cast<int>((hidden_size + BN - 1) / BN);
+    prev_ap.k3d = k3d;
     prev_tm_probs = tm_probs_out;
+    prev_tm_probs3 = tm_probs3;
   }
   return TALM_OK;
 }
