@@ -509,23 +509,26 @@ __global__ void __launch_bounds__(SLICE_THREADS, 1)
               tma_load_3d_pair(st + 2 * A_BYTES, &tm_weight3, lfull, 0,
                                ap.slice_row0 + kb0 * BK, (ht * BN + rank * (BN / 2)) / 64);
             }
-          } else
-          for (int j = 0; j < nsub; ++j) {
-            const int kb = kb0 + j;
-            uint8_t* a = smem + stage * STAGE_BYTES + j * SUB_BYTES;
-            if (unit.type == 0) {
-              int pr, ct;
-              logits_tile(lp, unit.tile, pr, ct);
-              tma_load_2d_pair(a, &tm_hidden, lfull, kb * BK, pr * PAIR_ROWS + rank * BM);
-              tma_load_2d_pair(a + A_BYTES, &tm_weight, lfull, kb * BK,
-                               lp.slice_row0 + ct * BN + rank * (BN / 2));
-            } else {
-              const int ht = unit.tile % ap.n_h_tiles, pr = unit.tile / ap.n_h_tiles;
-              tma_load_2d_pair(a, &tm_probs_in, lfull, kb * BK, pr * PAIR_ROWS + rank * BM);
+          } else {
+            // 2-D boxes, one sub-block at a time (an odd last sub-block, or a hidden size that
+            // is not a multiple of 64): A then B per sub-block
+            for (int j = 0; j < nsub; ++j) {
+              const int kb = kb0 + j;
+              uint8_t* a = st + j * SUB_BYTES;
+              if (unit.type == 0) {
+                int pr, ct;
+                logits_tile(lp, unit.tile, pr, ct);
+                tma_load_2d_pair(a, &tm_hidden, lfull, kb * BK, pr * PAIR_ROWS + rank * BM);
+                tma_load_2d_pair(a + A_BYTES, &tm_weight, lfull, kb * BK,
+                                 lp.slice_row0 + ct * BN + rank * (BN / 2));
+              } else {
+                const int ht = unit.tile % ap.n_h_tiles, pr = unit.tile / ap.n_h_tiles;
+                tma_load_2d_pair(a, &tm_probs_in, lfull, kb * BK, pr * PAIR_ROWS + rank * BM);
 #pragma unroll
-              for (int h = 0; h < BN / 2 / 64; ++h)
-                tma_load_2d_pair(a + A_BYTES + h * (64 * BK * 2), &tm_weight_mn, lfull,
-                                 ht * BN + rank * (BN / 2) + h * 64, ap.slice_row0 + kb * BK);
+                for (int h = 0; h < BN / 2 / 64; ++h)
+                  tma_load_2d_pair(a + A_BYTES + h * (64 * BK * 2), &tm_weight_mn, lfull,
+                                   ht * BN + rank * (BN / 2) + h * 64, ap.slice_row0 + kb * BK);
+              }
             }
           }
           ++issued;
