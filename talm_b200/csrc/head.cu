@@ -570,7 +570,8 @@ __global__ void __launch_bounds__(SLICE_THREADS, 1)
 #pragma unroll
               for (int k = 0; k < BK / 16; ++k)
                 // A: K-major rows of 128 B, +32 B per 16 K. B: MN-major, two 64-wide hidden
-                // groups of BK rows x 128 B (LBO = 8 KiB), 16 K-rows = +2 KiB.
+                // groups of 128 B rows (LBO = the group distance: 8 KiB for a 2-D stage, 16 KiB
+                // for a 3-D one), 16 K-rows = +2 KiB.
                 umma_f16_pair(d, smem_desc_sw128(a + k * 32, 16, 1024),
                               smem_desc_sw128(b + k * 2048, lbo_acc, 1024), kIdescAccum,
                               !first_kb || k != 0);
