@@ -231,10 +231,13 @@ def test_compaction_matches_full_accumulator(monkeypatch, n_tokens, vocab, unlab
     assert (outs["compact"][4][targets < 0] == 0).all()
 
 
-@pytest.mark.parametrize("size", [8, 40, 77, 100, 255])
+@pytest.mark.parametrize("size", [8, 40, 77, 100, 192, 255, 320])
 def test_odd_hidden_sizes_and_layouts(size):
     """Hidden sizes that are not multiples of 8 / 64, an fp32 weight, a padded-row weight and a
-    bf16 hidden (the wrapper casts and pads; the kernels see fp16 TMA rows)."""
+    bf16 hidden (the wrapper casts and pads; the kernels see fp16 TMA rows). 192 and 320 are
+    odd numbers of 64-column blocks: their walks mix two-sub-block stages fetched by one 3-D
+    request per operand with a last stage of one sub-block fetched by 2-D boxes, and their
+    accumulator tiles reach past the last weight column group."""
     torch.manual_seed(size)
     n, vocab = 90, 3000
     hidden = torch.randn(n, size, device=DEV, dtype=torch.bfloat16)
