@@ -18,7 +18,10 @@ weight rows [col0_r, col0_r + cols_r). Every rank holds the full hidden states a
 On CUDA ranks that can map each other's memory (one node, NVLink) steps 2-5 run as the peer
 exchange of the library (`PeerExchange`, talm_head_publish_stats ... talm_head_gather_finish):
 kernels write the statistics and the gradient rows straight into the other GPUs' buffers, each
-row is reduced once by its owner and the fp16 result is written to every rank. Otherwise
+row is reduced once by its owner and the fp16 result is written to every rank. Step 1 then stops
+before its last accumulator GEMM (talm_head_shard_begin), which runs after the merge
+(talm_head_shard_finish_scatter) and performs step 4 in its epilogue: each finished gradient
+row piece leaves for its owner while the tensor cores work on the remaining tiles. Otherwise
 (TALM_B200_PEER_EXCHANGE=0, or ranks that cannot map each other's memory) step 2 is an NCCL
 all_gather and step 5 an all_reduce of the fp32 gradient.
 
