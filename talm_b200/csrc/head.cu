@@ -29,6 +29,13 @@
 // A last launch (head_finalize_kernel) turns the statistics into loss / entropy / correctness
 // and the accumulator into dH = acc / s - fp16(W[target]) (fused_head.py:111-125, :160-169),
 // writing rows in the caller's original order.
+//
+// Operands reach shared memory in stages of two 64-column K sub-blocks (one barrier wait and
+// one commit per 128 of K), each operand of a stage by one 3-D TMA request where the hidden
+// size allows. In the vocabulary-parallel walk under the peer exchange, the walk's last step
+// (the accumulator GEMM of the last slice) can run after the ranks' statistics are merged
+// (talm_head_shard_begin / talm_head_shard_finish_scatter): its epilogue then finishes each
+// gradient row piece and stores it at the rank that owns the row.
 #include <math.h>
 
 #include <algorithm>
